@@ -1,0 +1,131 @@
+/*
+ * gdn_b200 C ABI: chunked gated-delta-rule (gated DeltaNet) prefill with a fused
+ * gated-RMSNorm epilogue, for NVIDIA B200 (sm_100a).
+ *
+ * Drop-in for the reference's kernel C ABI (kernels/chunk_delta_cuda.h:39-55 and
+ * its twin kernels/chunk_delta_cuda_tco.h:39-55): same names, argument order,
+ * types and error convention. All buffers are caller-owned, contiguous device
+ * memory; calls are asynchronous and stream-ordered; nothing is allocated.
+ *
+ * IO contract (unchanged from kernels/chunk_delta_cuda.h:11-27):
+ *   q, k : bf16 [B, T, HQK, DK]   pre-L2-normalised; v-head h reads qk-head h / (HV/HQK)
+ *   v    : bf16 [B, T, HV, DV]
+ *   g    : fp32 [B, T, HV]        log-decay (<= 0), cumsummed inside 64-token chunks
+ *   beta : fp32 [B, T, HV]
+ *   o    : bf16 [B, T, HV, DV]    out
+ *   s0   : fp32 [B, HV, DK, DV] or NULL (zeros);   sf : fp32 [B, HV, DK, DV] out
+ * The kernel applies the 1/sqrt(DK) query scale itself
+ * (kernels/chunk_delta_cuda.cu:805,811). Only DK = DV = 128 and chunk_size = 64
+ * are supported; anything else returns cudaErrorInvalidValue.
+ *
+ * Errors: cudaErrorInvalidValue for unsupported dimensions, HV % HQK != 0, NULL
+ * required pointers, a NULL or short workspace, or misaligned pointers
+ * (tensors must be 16-byte aligned); otherwise the launch error, if any.
+ * A device-side status word in the workspace records bounded-wait timeouts
+ * (read it with deltanet_read_status).
+ */
+#ifndef GDN_B200_GDN_PREFILL_H_
+#define GDN_B200_GDN_PREFILL_H_
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Workspace bytes for one prefill call (status header). Replaces
+ * deltanet_prefill_workspace_size, kernels/chunk_delta_cuda.h:40. The fused
+ * kernel keeps every chunk intermediate on chip, so the size no longer scales
+ * with B*HV*NC (the reference needs ~123 MB at B=1, T=1141, HV=32). */
+size_t deltanet_prefill_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size);
+
+/* Workspace bytes when dump_debug != 0: the header plus one fp32 record per
+ * (b, h, chunk) = [c(64) | T(64x64) | W(64x128) | v_new(64x128) | o(64x128) |
+ * S_entry(128x128)]. No counterpart in the reference (its debug dumps are
+ * always carried in the workspace, kernels/chunk_delta_cuda.cu:688-697). */
+size_t deltanet_prefill_debug_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size);
+
+/* Chunked gated delta rule prefill, o written in bf16. Replaces
+ * deltanet_chunk_prefill, kernels/chunk_delta_cuda.h:46-55 (identical signature). */
+cudaError_t deltanet_chunk_prefill(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    void* o,
+    const float* initial_state,
+    float* final_state,
+    int B, int T, int HV, int HQK, int DK, int DV, int chunk_size,
+    void* workspace, size_t workspace_bytes,
+    cudaStream_t stream, int dump_debug);
+
+/* The reference's production ("TCO", bf16 o-pass) entry points,
+ * kernels/chunk_delta_cuda_tco.h:40-55. Same math and contract; aliases of the
+ * two functions above. */
+size_t deltanet_tcop_prefill_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size);
+cudaError_t deltanet_tcop_chunk_prefill(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    void* o,
+    const float* initial_state,
+    float* final_state,
+    int B, int T, int HV, int HQK, int DK, int DV, int chunk_size,
+    void* workspace, size_t workspace_bytes,
+    cudaStream_t stream, int dump_debug);
+
+/* Prefill with the gated RMSNorm fused as the epilogue: o never reaches HBM.
+ *   y = bf16( w * bf16(o * rsqrt(mean(o^2) + eps)) * silu(z) ), o = bf16(gdn output)
+ * z, y : bf16 [B, T, HV, DV];  norm_w : bf16 [DV].
+ * Replaces the prefill + gated_rmsnorm plugin pair
+ * (kernels/chunk_delta_cuda.h:46 followed by gatedRmsNormKernel.h:16 /
+ * the TRT plugin gated_rmsnorm v1, gatedRmsNormPlugin.cpp:36-42). */
+cudaError_t deltanet_chunk_prefill_gated(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    const void* z, const void* norm_w, float eps,
+    void* y,
+    const float* initial_state,
+    float* final_state,
+    int B, int T, int HV, int HQK, int DK, int DV, int chunk_size,
+    void* workspace, size_t workspace_bytes,
+    cudaStream_t stream);
+
+/* Packed variable-length prefill: B = 1, T = total tokens, N sequences at
+ * int32 offsets cu_seqlens[0..N] (cu_seqlens[0] = 0, non-decreasing,
+ * cu_seqlens[N] = T). Each sequence starts from initial_states[i] (or zeros)
+ * and writes final_states[i] ([N, HV, DK, DV] fp32). If z and norm_w are both
+ * non-NULL the gated RMSNorm is fused and `out` receives y, else `out` receives o.
+ * No counterpart in the reference, whose adapter is exact-T and ignores
+ * context_lengths (gdnChunkPrefillSm87.h:16-19). */
+cudaError_t deltanet_chunk_prefill_varlen(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    const void* z, const void* norm_w, float eps,
+    void* out,
+    const float* initial_states,
+    float* final_states,
+    const int* cu_seqlens, int N,
+    int T, int HV, int HQK, int DK, int DV, int chunk_size,
+    void* workspace, size_t workspace_bytes,
+    cudaStream_t stream);
+
+/* Standalone gated RMSNorm over rows of dv: y = w * round(o * rsqrt(mean(o^2)+eps)) * silu(z).
+ * dtype 0 = fp16 I/O (the reference plugin's only format,
+ * gatedRmsNormPlugin.cpp:155-167), 1 = bf16 I/O. Replaces
+ * kernel::gatedRmsNormForward, gatedRmsNormKernel.h:16. */
+cudaError_t gated_rmsnorm_forward(const void* o, const void* z, const void* w, void* y,
+                                  int64_t rows, int dv, float eps, int dtype, cudaStream_t stream);
+
+/* Copy the device status word of a workspace to *status_host (synchronises
+ * `stream`). 0 = clean; bit 0 = a bounded wait timed out. Clears it when
+ * clear != 0. No counterpart in the reference (its kernels have no waits). */
+cudaError_t deltanet_read_status(void* workspace, int* status_host, int clear, cudaStream_t stream);
+
+/* Library build identifier (for logs and tests). */
+const char* gdn_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_GDN_PREFILL_H_ */

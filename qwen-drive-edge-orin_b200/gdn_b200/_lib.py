@@ -1,0 +1,78 @@
+"""Loader for the C-ABI shared library ``libgdn_b200.so`` (declared in include/gdn_prefill.h).
+
+The library is built in-tree by ``build.py`` (nvcc, sm_100a). Loading fails
+with :class:`GdnLibraryError` when it is missing: there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+_LIB_NAME = "libgdn_b200.so"
+_lock = threading.Lock()
+_lib = None
+
+c_void_p, c_int, c_float, c_size_t, c_int64 = (ctypes.c_void_p, ctypes.c_int, ctypes.c_float,
+                                               ctypes.c_size_t, ctypes.c_int64)
+
+# name -> (restype, argtypes); mirrors include/gdn_prefill.h
+SIGNATURES = {
+    "deltanet_prefill_workspace_size": (c_size_t, [c_int] * 6),
+    "deltanet_prefill_debug_workspace_size": (c_size_t, [c_int] * 6),
+    "deltanet_tcop_prefill_workspace_size": (c_size_t, [c_int] * 6),
+    "deltanet_chunk_prefill": (c_int, [c_void_p] * 8 + [c_int] * 7 + [c_void_p, c_size_t, c_void_p, c_int]),
+    "deltanet_tcop_chunk_prefill": (c_int, [c_void_p] * 8 + [c_int] * 7 + [c_void_p, c_size_t, c_void_p, c_int]),
+    "deltanet_chunk_prefill_gated": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p, c_void_p]
+                                     + [c_int] * 7 + [c_void_p, c_size_t, c_void_p]),
+    "deltanet_chunk_prefill_varlen": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p, c_void_p,
+                                                               c_void_p, c_int] + [c_int] * 6
+                                      + [c_void_p, c_size_t, c_void_p]),
+    "gated_rmsnorm_forward": (c_int, [c_void_p] * 4 + [c_int64, c_int, c_float, c_int, c_void_p]),
+    "deltanet_read_status": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
+    "gdn_b200_version": (ctypes.c_char_p, []),
+}
+
+
+class GdnLibraryError(RuntimeError):
+    """The CUDA library is missing or does not export the expected symbols."""
+
+
+def library_path() -> Path:
+    return _HERE / _LIB_NAME
+
+
+def load_library():
+    """Load (once) and return the ctypes handle with typed signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if not path.exists():
+            raise GdnLibraryError(f"{path} is not built; run qwen-drive-edge-orin_b200/build.py "
+                                  "(there is no CPU fallback for this path)")
+        lib = ctypes.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            try:
+                fn = getattr(lib, name)
+            except AttributeError as e:  # pragma: no cover - build mismatch
+                raise GdnLibraryError(f"{path} does not export {name}") from e
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def cuda_error_string(code: int) -> str:
+    try:
+        import torch  # noqa: F401
+        rt = ctypes.CDLL("libcudart.so.12")
+        rt.cudaGetErrorString.restype = ctypes.c_char_p
+        rt.cudaGetErrorString.argtypes = [ctypes.c_int]
+        return rt.cudaGetErrorString(code).decode()
+    except OSError:
+        return f"cudaError {code}"

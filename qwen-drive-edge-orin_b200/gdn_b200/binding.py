@@ -1,0 +1,260 @@
+"""Torch-facing binding over the C ABI (include/gdn_prefill.h).
+
+Mirrors the reference's pybind wrapper ``kernels/torch_binding.cpp``:
+``chunk_prefill(q, k, v, g, beta, s0=None) -> [o, sf]`` with the same input
+checks (:89-101: CUDA tensors, bf16 q/k/v, fp32 g/beta, ranks 4/4/3), the same
+s0 handling (:45-48: converted to contiguous fp32) and an error raised on any
+non-success return (:55). ``chunk_prefill_debug`` returns the per-chunk
+intermediates like the reference's debug entry (:57-84), in this kernel's own
+record layout. Calls go through ctypes to ``libgdn_b200.so`` on torch's current
+CUDA stream; outputs and the workspace are allocated with torch.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from ._lib import cuda_error_string, load_library
+
+__all__ = ["chunk_prefill", "chunk_prefill_debug", "chunk_prefill_gated", "chunk_prefill_varlen",
+           "gated_rmsnorm", "chunk_gated_delta_rule_fast", "workspace_size", "GdnError", "read_status"]
+
+CHUNK = 64
+HEAD_DIM = 128
+DBG_REC = 64 + 4096 + 3 * 8192 + 16384
+
+
+class GdnError(RuntimeError):
+    """A C-ABI call returned a CUDA error."""
+
+
+def _check(code: int, what: str):
+    if code != 0:
+        raise GdnError(f"{what} failed: {cuda_error_string(code)} ({code})")
+
+
+def _ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+_ws_lock = threading.Lock()
+_ws_cache: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device workspace (status header), zeroed on first use and reused."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _ws_cache.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _ws_cache[key] = ws
+        return ws
+
+
+def workspace_size(B: int, T: int, HV: int, debug: bool = False) -> int:
+    lib = load_library()
+    fn = lib.deltanet_prefill_debug_workspace_size if debug else lib.deltanet_prefill_workspace_size
+    return int(fn(B, T, HV, HEAD_DIM, HEAD_DIM, CHUNK))
+
+
+def read_status(device=None, clear: bool = True) -> int:
+    """Device status word of the cached workspace (0 = clean; bit 0 = a bounded wait timed out)."""
+    lib = load_library()
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    ws = _workspace(dev, 256)
+    out = ctypes.c_int(0)
+    _check(lib.deltanet_read_status(_ptr(ws), ctypes.byref(out), int(clear), _stream()), "deltanet_read_status")
+    return out.value
+
+
+def _check_inputs(q, k, v, g, beta, varlen=False):
+    if not all(t.is_cuda for t in (q, k, v, g, beta)):
+        raise ValueError("all inputs must be CUDA tensors")
+    if not (q.dtype == k.dtype == v.dtype == torch.bfloat16):
+        raise ValueError("q/k/v must be bf16")
+    if g.dtype != torch.float32 or beta.dtype != torch.float32:
+        raise ValueError("g/beta must be fp32")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4 or g.dim() != 3 or beta.dim() != 3:
+        raise ValueError("bad ranks: q/k/v must be 4-D [B,T,H,D], g/beta 3-D [B,T,HV]")
+    B, T, HQK, DK = q.shape
+    HV, DV = v.shape[2], v.shape[3]
+    if k.shape != q.shape or v.shape[:2] != (B, T) or g.shape != (B, T, HV) or beta.shape != (B, T, HV):
+        raise ValueError("shape mismatch between q/k/v/g/beta")
+    if HQK <= 0 or HV % HQK != 0:
+        raise ValueError("HV must be a multiple of HQK")
+    if DK != HEAD_DIM or DV != HEAD_DIM:
+        raise ValueError("only DK = DV = 128 is supported")
+    if varlen and B != 1:
+        raise ValueError("varlen inputs are packed: B must be 1")
+    return B, T, HQK, HV
+
+
+def _state(s0, shape, device):
+    if s0 is None:
+        return None
+    s0 = s0.to(device=device, dtype=torch.float32).contiguous()
+    if tuple(s0.shape) != tuple(shape):
+        raise ValueError(f"initial state must have shape {tuple(shape)}, got {tuple(s0.shape)}")
+    return s0
+
+
+def _run_prefill(q, k, v, g, beta, s0, debug: bool):
+    B, T, HQK, HV = _check_inputs(q, k, v, g, beta)
+    lib = load_library()
+    q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
+    dev = q.device
+    o = torch.empty_like(v)
+    sf = torch.empty(B, HV, HEAD_DIM, HEAD_DIM, device=dev, dtype=torch.float32)
+    s0 = _state(s0, (B, HV, HEAD_DIM, HEAD_DIM), dev)
+    if debug:
+        nbytes = workspace_size(B, T, HV, debug=True)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    else:
+        nbytes = workspace_size(B, T, HV)
+        ws = _workspace(dev, nbytes)
+    code = lib.deltanet_chunk_prefill(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(o), _ptr(s0),
+                                      _ptr(sf), B, T, HV, HQK, HEAD_DIM, HEAD_DIM, CHUNK, _ptr(ws),
+                                      ws.numel(), _stream(), int(debug))
+    _check(code, "deltanet_chunk_prefill")
+    if not debug:
+        return [o, sf]
+    NC = (T + CHUNK - 1) // CHUNK
+    rec = ws[256:256 + B * HV * NC * DBG_REC * 4].view(torch.float32).view(B, HV, NC, DBG_REC)
+    off = 0
+    views = []
+    for n, shp in (("c", (CHUNK,)), ("T", (CHUNK, CHUNK)), ("W", (CHUNK, HEAD_DIM)),
+                   ("v_new", (CHUNK, HEAD_DIM)), ("o", (CHUNK, HEAD_DIM)), ("S_entry", (HEAD_DIM, HEAD_DIM))):
+        sz = 1
+        for d in shp:
+            sz *= d
+        views.append(rec[..., off:off + sz].reshape(B, HV, NC, *shp))
+        off += sz
+    return [o, sf, *views]
+
+
+def chunk_prefill(q, k, v, g, beta, s0=None):
+    """Chunked gated delta rule prefill: returns [o (bf16 [B,T,HV,128]), final_state (fp32 [B,HV,128,128])].
+
+    Same contract as the reference binding ``chunk_prefill`` (kernels/torch_binding.cpp:113-117):
+    q/k bf16 [B,T,HQK,128] pre-L2-normalised, v bf16 [B,T,HV,128], g/beta fp32 [B,T,HV],
+    optional s0 fp32 [B,HV,128,128]; the 1/sqrt(128) query scale is applied inside.
+    """
+    return _run_prefill(q, k, v, g, beta, s0, debug=False)
+
+
+def chunk_prefill_debug(q, k, v, g, beta, s0=None):
+    """[o, sf, c, T, W, v_new, o_fp32, S_entry]: per-chunk intermediates, each [B, HV, NC, ...].
+
+    The reference's debug entry (kernels/torch_binding.cpp:119-124) exposes its
+    scratch views; this kernel keeps intermediates on chip, so the debug call
+    asks it to dump them: in-chunk cumsum c, T = (I+L)^-1, W = T diag(beta e^c) K,
+    v_new = U - W S, o before rounding, and the chunk-entry state.
+    """
+    return _run_prefill(q, k, v, g, beta, s0, debug=True)
+
+
+def chunk_prefill_gated(q, k, v, g, beta, z, w, s0=None, eps: float = 1e-6):
+    """Prefill with the gated RMSNorm fused: returns [y (bf16 [B,T,HV,128]), final_state].
+
+    y = bf16(w * bf16(o * rsqrt(mean(o^2) + eps)) * silu(z)) with o the bf16 GDN output,
+    the semantics of the reference's gated_rmsnorm plugin (gatedRmsNormKernel.cu:21-54).
+    """
+    B, T, HQK, HV = _check_inputs(q, k, v, g, beta)
+    if not (z.is_cuda and w.is_cuda) or z.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("z and w must be bf16 CUDA tensors")
+    if tuple(z.shape) != tuple(v.shape) or tuple(w.shape) != (HEAD_DIM,):
+        raise ValueError("z must match v's shape and w must be [128]")
+    lib = load_library()
+    q, k, v, g, beta, z, w = (t.contiguous() for t in (q, k, v, g, beta, z, w))
+    dev = q.device
+    y = torch.empty_like(v)
+    sf = torch.empty(B, HV, HEAD_DIM, HEAD_DIM, device=dev, dtype=torch.float32)
+    s0 = _state(s0, (B, HV, HEAD_DIM, HEAD_DIM), dev)
+    ws = _workspace(dev, workspace_size(B, T, HV))
+    code = lib.deltanet_chunk_prefill_gated(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w),
+                                            float(eps), _ptr(y), _ptr(s0), _ptr(sf), B, T, HV, HQK, HEAD_DIM,
+                                            HEAD_DIM, CHUNK, _ptr(ws), ws.numel(), _stream())
+    _check(code, "deltanet_chunk_prefill_gated")
+    return [y, sf]
+
+
+def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, s0=None, z=None, w=None, eps: float = 1e-6):
+    """Packed variable-length prefill (B = 1): returns [o or y, final_states [N,HV,128,128]].
+
+    ``cu_seqlens`` is int32 [N+1] (on the device); sequence i covers tokens
+    [cu[i], cu[i+1]) and starts from s0[i] (or zeros). When z and w are given
+    the gated RMSNorm is fused and the first output is y.
+    """
+    _, T, HQK, HV = _check_inputs(q, k, v, g, beta, varlen=True)
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1 or not cu_seqlens.is_cuda:
+        raise ValueError("cu_seqlens must be a 1-D int32 CUDA tensor")
+    N = cu_seqlens.numel() - 1
+    if (z is None) != (w is None):
+        raise ValueError("pass both z and w (fused norm) or neither")
+    lib = load_library()
+    q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
+    cu = cu_seqlens.contiguous()
+    if z is not None:
+        z, w = z.contiguous(), w.contiguous()
+        if z.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or tuple(z.shape) != tuple(v.shape):
+            raise ValueError("z must be bf16 with v's shape and w bf16 [128]")
+    dev = q.device
+    out = torch.empty_like(v)
+    sf = torch.empty(N, HV, HEAD_DIM, HEAD_DIM, device=dev, dtype=torch.float32)
+    s0 = _state(s0, (N, HV, HEAD_DIM, HEAD_DIM), dev)
+    ws = _workspace(dev, workspace_size(1, T, HV))
+    code = lib.deltanet_chunk_prefill_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w),
+                                             float(eps), _ptr(out), _ptr(s0), _ptr(sf), _ptr(cu), N, T, HV, HQK,
+                                             HEAD_DIM, HEAD_DIM, CHUNK, _ptr(ws), ws.numel(), _stream())
+    _check(code, "deltanet_chunk_prefill_varlen")
+    return [out, sf]
+
+
+def gated_rmsnorm(o, z, w, eps: float = 1e-6):
+    """Standalone gated RMSNorm over the last dim (fp16 or bf16 I/O): the reference's
+    ``kernel::gatedRmsNormForward`` (gatedRmsNormKernel.h:16) / ``gated_rmsnorm`` plugin."""
+    if o.dtype not in (torch.float16, torch.bfloat16) or z.dtype != o.dtype or w.dtype != o.dtype:
+        raise ValueError("o, z, w must share dtype fp16 or bf16")
+    if tuple(z.shape) != tuple(o.shape) or w.dim() != 1 or w.shape[0] != o.shape[-1]:
+        raise ValueError("z must match o and w must be [dv]")
+    if not (o.is_cuda and z.is_cuda and w.is_cuda):
+        raise ValueError("all inputs must be CUDA tensors")
+    lib = load_library()
+    o, z, w = o.contiguous(), z.contiguous(), w.contiguous()
+    y = torch.empty_like(o)
+    dv = o.shape[-1]
+    rows = o.numel() // dv if dv else 0
+    code = lib.gated_rmsnorm_forward(_ptr(o), _ptr(z), _ptr(w), _ptr(y), rows, dv, float(eps),
+                                     0 if o.dtype == torch.float16 else 1, _stream())
+    _check(code, "gated_rmsnorm_forward")
+    return y
+
+
+def _l2norm_fp32(x):
+    inv = torch.rsqrt((x.float() * x.float()).sum(-1, keepdim=True) + 1e-6)
+    return (x.float() * inv).to(torch.bfloat16)
+
+
+def chunk_gated_delta_rule_fast(query, key, value, g, beta, chunk_size=64, initial_state=None,
+                                output_final_state=True, use_qk_l2norm_in_kernel=False):
+    """transformers-compatible signature (the reference's twin,
+    kernels/harness/chunk_delta.py:361-368): returns (o, final_state or None).
+
+    q/k may carry HQK heads (grouped) or HV heads; with use_qk_l2norm_in_kernel
+    they are L2-normalised in fp32 and rounded to bf16 first, as the
+    reference's adapter does (gdnChunkPrefillSm87.cu:52-85).
+    """
+    if chunk_size != CHUNK:
+        raise ValueError("only chunk_size=64 is supported")
+    if use_qk_l2norm_in_kernel:
+        query, key = _l2norm_fp32(query), _l2norm_fp32(key)
+    o, sf = chunk_prefill(query.to(torch.bfloat16), key.to(torch.bfloat16), value.to(torch.bfloat16),
+                          g.float(), beta.float(), initial_state)
+    return o, (sf if output_final_state else None)
