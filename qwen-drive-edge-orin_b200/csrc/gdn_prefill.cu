@@ -10,16 +10,18 @@
 //       substitution (CUDA cores, fp32)
 //   P3  W^T  = K^T (T diag(beta e^c))^T                              tcgen05, M=128
 //   C12 v_new^T = v^T (T diag(beta))^T - S^T W^T                    tcgen05, M=128
-//   C3  o^T  = S^T (scale e^c q)^T + v_new^T M^T                     tcgen05, M=128
+//   C3  o^T  = scale e^c (S^T q^T) + v_new^T M^T  (two accumulators)  tcgen05, M=128
 //   C4  dS^T = (v_new e^{c_L-c})^T K                                 tcgen05, M=128, N=128
 //   --  S <- e^{c_L} S + dS (fp32 registers); o -> gated RMSNorm -> y
 // Transposed forms put the 128-wide feature dimension on the MMA M axis so
 // every accumulator row is one TMEM lane, which makes the state update and
 // the norm epilogue thread-local.
 //
-// Precision: every operand that is not already a bf16 input (S, W, T') is
-// split into bf16 hi + lo parts so the fp32 state path keeps ~16 mantissa
+// Precision: every operand that is not already a bf16 input (S, W, T', T'',
+// v_new, M) is split into bf16 hi + lo parts, so products keep ~16 mantissa
 // bits; accumulation is fp32 in TMEM; the state itself is fp32 in registers.
+// Exact bf16 inputs (q, k, v) enter the MMAs unscaled; per-token factors
+// (e^c, e^{c_L-c}) are applied in fp32 around them.
 //
 // Semantics follow the reference's torch chunked fallback
 // (kernels/harness/parity_test.py:35-96) and its CUDA kernels
@@ -61,15 +63,16 @@ constexpr uint32_t OFF_TPP_HI = OFF_X + 16384;  //  T'' = T diag(beta e^c)    [6
 constexpr uint32_t OFF_TPP_LO = OFF_X + 24576;
 constexpr uint32_t OFF_W_HI = OFF_X + 32768;    //  W   [64 tok][128 dk]  (8 KB/panel)
 constexpr uint32_t OFF_W_LO = OFF_X + 49152;
-constexpr uint32_t OFF_VN = OFF_X + 0;          //  v_new^T          [128 dv][64 tok]
+constexpr uint32_t OFF_VN = OFF_X + 0;          //  v_new^T hi       [128 dv][64 tok]
 constexpr uint32_t OFF_VNP_HI = OFF_X + 16384;  //  (v_new e^{cL-c})^T hi
 constexpr uint32_t OFF_VNP_LO = OFF_X + 32768;  //                     lo
+constexpr uint32_t OFF_VN_LO = OFF_X + 49152;   //  v_new^T lo
 constexpr uint32_t OFF_XTMP = OFF_X + 0;        //  inversion scratch [3][16][16] fp32
-constexpr uint32_t OFF_M = 196608;       // M = scale (q k^T) * decay, [64][64] bf16
-constexpr uint32_t OFF_L = 204800;       // L / T fp32 [64][65]; later Qg tile (8 KB/panel)
-constexpr uint32_t OFF_QG = OFF_L;
+constexpr uint32_t OFF_L = 196608;       // L / T fp32 [64][65]; later M hi/lo
+constexpr uint32_t OFF_M_HI = OFF_L;     // M = scale (q k^T) * decay, [64][64] bf16
+constexpr uint32_t OFF_M_LO = OFF_L + 8192;
 constexpr int LSTRIDE = 65;
-constexpr uint32_t OFF_MISC = OFF_L + 64 * LSTRIDE * 4;  // 221440
+constexpr uint32_t OFF_MISC = OFF_L + 64 * LSTRIDE * 4;  // 213248
 constexpr uint32_t MISC_C = 0;      // c        [64] f32
 constexpr uint32_t MISC_BETA = 256; // beta     [64]
 constexpr uint32_t MISC_EC = 512;   // e^c      [64]
@@ -90,6 +93,7 @@ constexpr uint32_t TM_W = 64;    // W^T          64 cols
 constexpr uint32_t TM_V = 128;   // v_new^T      64 cols
 constexpr uint32_t TM_O = 192;   // o^T          64 cols
 constexpr uint32_t TM_S = 256;   // dS^T        128 cols
+constexpr uint32_t TM_O2 = 384;  // v_new^T M^T  64 cols
 
 // Barrier slots.
 enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4 };
@@ -348,7 +352,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     constexpr uint32_t ID_W = ptx::idesc_bf16(128, 64, 1, 0, 0);    // K^T T''^T   (A MN-major)
     constexpr uint32_t ID_U = ptx::idesc_bf16(128, 64, 1, 0, 0);    // v^T T'^T    (A MN-major)
     constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 64, 0, 0, 1);   // -S^T W^T
-    constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T Qg^T, v_new^T M^T
+    constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T q^T, v_new^T M^T
     constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K  (B MN-major)
 
     for (int n = 0; n < NC; ++n) {
@@ -403,19 +407,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             float v[32];
             ptx::tmem_ld32(tmem + lane_addr + TM_P + 32 * half, v);
             ptx::tmem_wait_ld();
-            if (row < CS) {  // M row i = row: scale * q_i.k_j * e^{c_i - c_j}, j <= i
-                const int i = row;
-                const float ci = c_s[i];
-                float m[32];
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int j = 32 * half + jj;
-                    m[jj] = (j <= i) ? v[jj] * p.scale * expf(ci - c_s[j]) : 0.f;
-                }
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch)
-                    put8_split(sb + OFF_M + sw_chunk(i, 4 * half + ch, 64), 0, m + 8 * ch, false);
-            } else {  // L row i: beta_i k_i.k_j e^{c_i - c_j}, j < i
+            // rows 0-63 (q.k) stay in TMEM until M is formed after C12
+            if (row >= CS) {  // L row i: beta_i k_i.k_j e^{c_i - c_j}, j < i
                 const int i = row - CS;
                 const float ci = c_s[i], bi = beta_s[i];
 #pragma unroll
@@ -472,23 +465,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ptx::mma_commit(bar(BAR_MMA));
             ++issued[BAR_MMA];
         }
-        // Meanwhile: Qg = bf16(q * scale * e^c) into the (now free) L region.
-        for (int e = tid; e < CS * 16; e += NTHREADS) {
-            const int r = e >> 4, ch = e & 15;
-            uint32_t w4[4];
-            ld_shared_v4(sb + OFF_QK + (ch >> 3) * 16384 + r * 128 + (((ch & 7) ^ (r & 7)) << 4), w4[0],
-                         w4[1], w4[2], w4[3]);
-            const float f = p.scale * ec_s[r];
-            float x[8];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                __nv_bfloat162 b2 = *reinterpret_cast<__nv_bfloat162*>(&w4[u]);
-                x[2 * u] = __bfloat162float(b2.x) * f;
-                x[2 * u + 1] = __bfloat162float(b2.y) * f;
-            }
-            put8_split(sb + OFF_QG + sw_chunk(r, ch, 64), 0, x, false);
-        }
-        ptx::fence_proxy_async_smem();
         wait_mma();
         {
             float v[32];
@@ -515,7 +491,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::fence_proxy_async_smem();
         __syncthreads();
         if (*abort_flag) break;
-        if (tid == 0 && n + 1 < NC) load_q(n + 1);  // q tile consumed (P1 done, Qg formed)
 
         // ---- C12: v_new^T = v^T T'^T - S^T W^T ----
         wait_bar(BAR_V, ph);
@@ -562,7 +537,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 const uint32_t co = sw_chunk(dv, 4 * half + ch, 128);
-                put8_split(sb + OFF_VN + co, 0, v + 8 * ch, false);
+                put8_split(sb + OFF_VN + co, sb + OFF_VN_LO + co, v + 8 * ch, true);
                 put8_split(sb + OFF_VNP_HI + co, sb + OFF_VNP_LO + co, vp + 8 * ch, true);
             }
             if (p.dbg) {
@@ -571,12 +546,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 for (int jj = 0; jj < 32; ++jj) rec[DBG_VN + (32 * half + jj) * HD + dv] = v[jj];
             }
         }
+        {   // M row i: scale * (q_i.k_j) * e^{c_i - c_j} for j <= i, hi/lo, from the P1 accumulator
+            float v[32];
+            ptx::tmem_ld32(tmem + lane_addr + TM_P + 32 * half, v);
+            ptx::tmem_wait_ld();
+            if (row < CS) {
+                const int i = row;
+                const float ci = c_s[i];
+                float m[32];
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int j = 32 * half + jj;
+                    m[jj] = (j <= i) ? v[jj] * p.scale * expf(ci - c_s[j]) : 0.f;
+                }
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    const uint32_t co = sw_chunk(i, 4 * half + ch, 64);
+                    put8_split(sb + OFF_M_HI + co, sb + OFF_M_LO + co, m + 8 * ch, true);
+                }
+            }
+        }
         ptx::tc_fence_before();
         ptx::fence_proxy_async_smem();
         __syncthreads();
         if (*abort_flag) break;
 
-        // ---- C3: o^T = S^T Qg^T + v_new^T M^T ; C4: dS^T = v_new'^T K ----
+        // ---- C3: o1^T = S^T q^T, o2^T = v_new^T M^T ; C4: dS^T = v_new'^T K ----
         if (tid == 0) {
             ptx::tc_fence_after();
 #pragma unroll
@@ -586,15 +581,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 for (int s = 0; s < 8; ++s) {
                     const uint64_t a =
                         ptx::sw128_desc(sb + sa + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
-                    const uint64_t b = ptx::sw128_desc(sb + OFF_QG + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024);
+                    const uint64_t b = ptx::sw128_desc(sb + OFF_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
                     ptx::mma_bf16(tmem + TM_O, a, b, ID_O, (part | s) > 0);
                 }
             }
+            // (VN_hi, M_hi), (VN_lo, M_hi), (VN_hi, M_lo)
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const uint64_t a = ptx::sw128_desc(sb + OFF_VN + s * 32, 16, 1024);
-                const uint64_t b = ptx::sw128_desc(sb + OFF_M + s * 32, 16, 1024);
-                ptx::mma_bf16(tmem + TM_O, a, b, ID_O, 1u);
+            for (int term = 0; term < 3; ++term) {
+                const uint32_t va = (term == 1) ? OFF_VN_LO : OFF_VN;
+                const uint32_t mb = (term == 2) ? OFF_M_LO : OFF_M_HI;
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const uint64_t a = ptx::sw128_desc(sb + va + s * 32, 16, 1024);
+                    const uint64_t b = ptx::sw128_desc(sb + mb + s * 32, 16, 1024);
+                    ptx::mma_bf16(tmem + TM_O2, a, b, ID_O, (term | s) > 0);
+                }
             }
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
@@ -610,7 +611,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ++issued[BAR_MMA];
         }
         wait_mma();
-        if (tid == 0 && n + 1 < NC) load_k(n + 1);  // k tile consumed
+        if (tid == 0 && n + 1 < NC) {  // q and k tiles consumed
+            load_q(n + 1);
+            load_k(n + 1);
+        }
 
         // ---- state update: S <- e^{cL} S + dS ----
         {
@@ -636,10 +640,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 
         // ---- output: o (bf16) or the fused gated RMSNorm y ----
         {
-            float v[32];
+            float v[32], v2[32];
             ptx::tmem_ld32(tmem + lane_addr + TM_O + 32 * half, v);
+            ptx::tmem_ld32(tmem + lane_addr + TM_O2 + 32 * half, v2);
             ptx::tmem_wait_ld();
             const int dv = row;
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) v[jj] = fmaf(p.scale * ec_s[32 * half + jj], v[jj], v2[jj]);
             if (p.dbg) {
                 float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
 #pragma unroll

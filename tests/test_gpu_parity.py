@@ -93,7 +93,7 @@ def test_stages_against_oracle_intermediates():
     assert errs["W"] < 1e-3
     assert errs["S_entry"] < 1e-3
     assert errs["v_new"] < 1e-3
-    assert errs["o"] < 5e-3
+    assert errs["o"] < 1e-4
     check_o(o, o_ref, sf, sf_ref, "debug-run")
 
 
