@@ -8,14 +8,15 @@
 //   P1  [Q;K] K^T            -> q.k (rows 0-63) and k.k (rows 64-127)  tcgen05, M=128
 //   --  L, M = scale (q k^T) * decay  (registers), T by blocked forward
 //       substitution (CUDA cores, fp32)
-//   P3  W^T  = K^T (T diag(beta e^c))^T                              tcgen05, M=128
+//   P3  W    = (T diag(beta e^c)) K                                  tcgen05, M=64, N=128
 //   C12 v_new^T = v^T (T diag(beta))^T - S^T W^T                    tcgen05, M=128
 //   C3  o^T  = scale e^c (S^T q^T) + v_new^T M^T  (two accumulators)  tcgen05, M=128
 //   C4  dS^T = (v_new e^{c_L-c})^T K                                 tcgen05, M=128, N=128
 //   --  S <- e^{c_L} S + dS (fp32 registers); o -> gated RMSNorm -> y
 // Transposed forms put the 128-wide feature dimension on the MMA M axis so
-// every accumulator row is one TMEM lane, which makes the state update and
-// the norm epilogue thread-local.
+// every accumulator row is one TMEM lane, which makes the state update
+// thread-local; the norm epilogue re-reads o through a swizzled shared tile
+// with four threads per token and 16-byte loads and stores.
 //
 // Precision: every operand that is not already a bf16 input (S, W, T', T'',
 // v_new, M) is split into bf16 hi + lo parts, so products keep ~16 mantissa
@@ -71,14 +72,13 @@ constexpr uint32_t OFF_XTMP = OFF_X + 0;        //  inversion scratch [3][16][16
 constexpr uint32_t OFF_L = 196608;       // L / T fp32 [64][65]; later M hi/lo
 constexpr uint32_t OFF_M_HI = OFF_L;     // M = scale (q k^T) * decay, [64][64] bf16
 constexpr uint32_t OFF_M_LO = OFF_L + 8192;
+constexpr uint32_t OFF_OST = OFF_L;      // o staging [64 tok][128 dv] bf16 after C3 (8 KB/panel)
 constexpr int LSTRIDE = 65;
 constexpr uint32_t OFF_MISC = OFF_L + 64 * LSTRIDE * 4;  // 213248
 constexpr uint32_t MISC_C = 0;      // c        [64] f32
 constexpr uint32_t MISC_BETA = 256; // beta     [64]
 constexpr uint32_t MISC_EC = 512;   // e^c      [64]
 constexpr uint32_t MISC_ED = 768;   // e^{cL-c} [64]
-constexpr uint32_t MISC_RSTD = 1024;// rstd     [64]
-constexpr uint32_t MISC_RED = 1280; // [4][64]
 constexpr uint32_t MISC_BAR = 2304; // 6 mbarriers
 constexpr uint32_t MISC_TMEM = 2368;
 constexpr uint32_t MISC_FLAG = 2372;
@@ -89,11 +89,11 @@ static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory 
 
 // TMEM columns of the accumulators (all 128 lanes).
 constexpr uint32_t TM_P = 0;     // [Q;K]K^T     64 cols
-constexpr uint32_t TM_W = 64;    // W^T          64 cols
-constexpr uint32_t TM_V = 128;   // v_new^T      64 cols
-constexpr uint32_t TM_O = 192;   // o^T          64 cols
+constexpr uint32_t TM_V = 64;    // v_new^T      64 cols
+constexpr uint32_t TM_O = 128;   // S^T q^T      64 cols
+constexpr uint32_t TM_O2 = 192;  // v_new^T M^T  64 cols
 constexpr uint32_t TM_S = 256;   // dS^T        128 cols
-constexpr uint32_t TM_O2 = 384;  // v_new^T M^T  64 cols
+constexpr uint32_t TM_W = 384;   // W (M=64 layout: token rows in lanes 0-15 of each quarter), 128 cols
 
 // Barrier slots.
 enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4 };
@@ -218,6 +218,18 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid) 
     }
 }
 
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcpf(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+constexpr float LOG2E = 1.4426950408889634f;
+
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -225,7 +237,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     const uint32_t sb = ptx::smem_u32(smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3, half = warp >> 2;
-    const int row = quarter * 32 + lane;  // TMEM lane of this thread (dv / dk / token row)
+    const int row = quarter * 32 + lane;  // TMEM lane of this thread for M=128 accumulators
     const int h = blockIdx.y;
     const int seq = blockIdx.z;
     const int hq = h / (p.HV / p.HQK);
@@ -248,8 +260,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     float* beta_s = misc + MISC_BETA / 4;
     float* ec_s = misc + MISC_EC / 4;
     float* ed_s = misc + MISC_ED / 4;
-    float* rstd_s = misc + MISC_RSTD / 4;
-    float* red_s = misc + MISC_RED / 4;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + MISC_FLAG);
     const uint32_t bar0 = sb + OFF_MISC + MISC_BAR;
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
@@ -289,7 +299,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             put8_split(sb + OFF_SHI + sw_chunk(row, 8 * half + ch, 128),
                        sb + OFF_SLO + sw_chunk(row, 8 * half + ch, 128), S + 8 * ch, true);
     }
-    const float wgt = p.gated ? __bfloat162float(p.w[row]) : 0.f;
+    // Epilogue mapping: token et = tid / 4, dv slice [32*eq, 32*eq + 32).
+    const int et = tid >> 2, eq = tid & 3;
+    float wgt[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) wgt[j] = p.gated ? __bfloat162float(p.w[32 * eq + j]) : 0.f;
 
     // ---- TMA issue helpers (thread 0) ----
     uint32_t issued[5] = {0, 0, 0, 0, 0}, consumed[5] = {0, 0, 0, 0, 0};
@@ -344,16 +358,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         load_v(0);
         if (p.gated) load_z(0);
     }
+    // Gates of the next chunk are prefetched into warp 0's registers (lane l: tokens 2l, 2l+1).
+    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
+    auto load_gates = [&](int n) {
+        const int valid = min(CS, len - n * CS);
+        const long long t0 = tok_base + (long long)n * CS;
+        gn0 = gn1 = bn0 = bn1 = 0.f;
+        if (2 * lane < valid) {
+            gn0 = __ldg(p.g + (size_t)(t0 + 2 * lane) * p.HV + h);
+            bn0 = __ldg(p.beta + (size_t)(t0 + 2 * lane) * p.HV + h);
+        }
+        if (2 * lane + 1 < valid) {
+            gn1 = __ldg(p.g + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
+            bn1 = __ldg(p.beta + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
+        }
+    };
+    if (warp == 0 && NC > 0) load_gates(0);
     ptx::fence_proxy_async_smem();  // S tiles written by all threads
     __syncthreads();
 
-    // Descriptor constants.
+    // Instruction descriptors.
     constexpr uint32_t ID_P = ptx::idesc_bf16(128, 64, 0, 0, 0);    // [Q;K] K^T
-    constexpr uint32_t ID_W = ptx::idesc_bf16(128, 64, 1, 0, 0);    // K^T T''^T   (A MN-major)
-    constexpr uint32_t ID_U = ptx::idesc_bf16(128, 64, 1, 0, 0);    // v^T T'^T    (A MN-major)
+    constexpr uint32_t ID_W = ptx::idesc_bf16(64, 128, 0, 1, 0);    // T'' K        (B MN-major)
+    constexpr uint32_t ID_U = ptx::idesc_bf16(128, 64, 1, 0, 0);    // v^T T'^T     (A MN-major)
     constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 64, 0, 0, 1);   // -S^T W^T
     constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T q^T, v_new^T M^T
-    constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K  (B MN-major)
+    constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K   (B MN-major)
 
     for (int n = 0; n < NC; ++n) {
         if (*abort_flag) break;
@@ -361,30 +391,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         const long long tok0 = tok_base + (long long)n * CS;
         const uint32_t ph = (uint32_t)(n & 1);
 
-        // ---- gates: g, beta for this chunk; zero past the sequence end ----
-        if (tid < CS) {
-            float gv = 0.f, bv = 0.f;
-            if (tid < valid) {
-                const size_t gi = (size_t)(tok0 + tid) * p.HV + h;
-                gv = __ldg(p.g + gi);
-                bv = __ldg(p.beta + gi);
+        // ---- gates: in-chunk inclusive cumsum of g (warp scan), decay factors ----
+        if (warp == 0) {
+            const float g0 = gn0, g1 = gn1, b0 = bn0, b1 = bn1;
+            if (n + 1 < NC) load_gates(n + 1);  // overlaps the rest of this chunk
+            float s = g0 + g1;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const float t = __shfl_up_sync(0xffffffffu, s, off);
+                if (lane >= off) s += t;
             }
-            c_s[tid] = gv;
-            beta_s[tid] = bv;
-        }
-        __syncthreads();
-        if (tid == 0) {  // sequential in-chunk cumsum, same order as torch's cumsum
-            float acc = 0.f;
-            for (int i = 0; i < CS; ++i) {
-                acc += c_s[i];
-                c_s[i] = acc;
-            }
-        }
-        __syncthreads();
-        const float cL = c_s[CS - 1];
-        if (tid < CS) {
-            ec_s[tid] = expf(c_s[tid]);
-            ed_s[tid] = expf(cL - c_s[tid]);
+            const float c1 = s, c0 = s - g1;
+            const float cL = __shfl_sync(0xffffffffu, c1, 31);
+            c_s[2 * lane] = c0;
+            c_s[2 * lane + 1] = c1;
+            beta_s[2 * lane] = b0;
+            beta_s[2 * lane + 1] = b1;
+            ec_s[2 * lane] = ex2f(c0 * LOG2E);
+            ec_s[2 * lane + 1] = ex2f(c1 * LOG2E);
+            ed_s[2 * lane] = ex2f((cL - c0) * LOG2E);
+            ed_s[2 * lane + 1] = ex2f((cL - c1) * LOG2E);
         }
 
         // ---- P1: [Q;K] K^T ----
@@ -402,6 +428,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ptx::mma_commit(bar(BAR_MMA));
             ++issued[BAR_MMA];
         }
+        __syncthreads();  // c_s / beta_s visible
         wait_mma();
         {
             float v[32];
@@ -414,7 +441,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) {
                     const int j = 32 * half + jj;
-                    Ls[i * LSTRIDE + j] = (j < i) ? bi * v[jj] * expf(ci - c_s[j]) : 0.f;
+                    Ls[i * LSTRIDE + j] = (j < i) ? bi * v[jj] * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
                 }
             }
         }
@@ -449,7 +476,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::fence_proxy_async_smem();
         __syncthreads();
 
-        // ---- P3: W^T = K^T T''^T (hi + lo) ----
+        // ---- P3: W = T'' K (hi + lo), M = 64 tokens x N = 128 dk ----
         if (tid == 0) {
             ptx::tc_fence_after();
 #pragma unroll
@@ -457,8 +484,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint32_t tpp = part ? OFF_TPP_LO : OFF_TPP_HI;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const uint64_t a = ptx::sw128_desc(sb + OFF_QK + 8192 + s * 2048, 16384, 1024);
-                    const uint64_t b = ptx::sw128_desc(sb + tpp + s * 32, 16, 1024);
+                    const uint64_t a = ptx::sw128_desc(sb + tpp + s * 32, 16, 1024);
+                    const uint64_t b = ptx::sw128_desc(sb + OFF_QK + 8192 + s * 2048, 16384, 1024);
                     ptx::mma_bf16(tmem + TM_W, a, b, ID_W, (part | s) > 0);
                 }
             }
@@ -466,25 +493,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ++issued[BAR_MMA];
         }
         wait_mma();
-        {
-            float v[32];
-            ptx::tmem_ld32(tmem + lane_addr + TM_W + 32 * half, v);
-            ptx::tmem_wait_ld();
-            const int dk = row;
-            __nv_bfloat16* whi = reinterpret_cast<__nv_bfloat16*>(smem + OFF_W_HI);
-            __nv_bfloat16* wlo = reinterpret_cast<__nv_bfloat16*>(smem + OFF_W_LO);
+        {   // M=64 accumulator: token 16*quarter + lane (lanes 0-15), dk 64*half .. +63
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-                const int tok = 32 * half + jj;
-                const uint32_t off = sw_off(tok, dk, 64) >> 1;
-                const __nv_bfloat16 hb = __float2bfloat16_rn(v[jj]);
-                whi[off] = hb;
-                wlo[off] = __float2bfloat16_rn(v[jj] - __bfloat162float(hb));
-            }
-            if (p.dbg) {
-                float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
+            for (int c2 = 0; c2 < 2; ++c2) {
+                float v[32];
+                ptx::tmem_ld32(tmem + lane_addr + TM_W + 64 * half + 32 * c2, v);
+                ptx::tmem_wait_ld();
+                if (lane < 16) {
+                    const int tok = 16 * quarter + lane;
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) rec[DBG_W + (32 * half + jj) * HD + dk] = v[jj];
+                    for (int ch = 0; ch < 4; ++ch) {
+                        const uint32_t co = sw_chunk(tok, 8 * half + 4 * c2 + ch, 64);
+                        put8_split(sb + OFF_W_HI + co, sb + OFF_W_LO + co, v + 8 * ch, true);
+                    }
+                    if (p.dbg) {
+                        float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) rec[DBG_W + tok * HD + 64 * half + 32 * c2 + jj] = v[jj];
+                    }
+                }
             }
         }
         ptx::tc_fence_before();
@@ -557,7 +584,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) {
                     const int j = 32 * half + jj;
-                    m[jj] = (j <= i) ? v[jj] * p.scale * expf(ci - c_s[j]) : 0.f;
+                    m[jj] = (j <= i) ? v[jj] * p.scale * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
                 }
 #pragma unroll
                 for (int ch = 0; ch < 4; ++ch) {
@@ -638,7 +665,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                            sb + OFF_SLO + sw_chunk(row, 8 * half + ch, 128), S + 8 * ch, true);
         }
 
-        // ---- output: o (bf16) or the fused gated RMSNorm y ----
+        // ---- o = scale e^c o1 + o2, rounded to bf16, staged [tok][dv] (M tiles are dead) ----
         {
             float v[32], v2[32];
             ptx::tmem_ld32(tmem + lane_addr + TM_O + 32 * half, v);
@@ -652,53 +679,69 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) rec[DBG_O + (32 * half + jj) * HD + dv] = v[jj];
             }
+            __nv_bfloat16* ot = reinterpret_cast<__nv_bfloat16*>(smem + OFF_OST);
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) v[jj] = bf16r(v[jj]);
-            const size_t ostride = (size_t)p.HV * HD;
-            __nv_bfloat16* obase = p.out + (size_t)tok0 * ostride + (size_t)h * HD + dv;
-            if (!p.gated) {
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int tok = 32 * half + jj;
-                    if (tok < valid) obase[(size_t)tok * ostride] = __float2bfloat16_rn(v[jj]);
-                }
-            } else {
-                // Sum of squares per token over the 128 dv lanes: butterfly
-                // reduce-scatter inside the warp, then the 4 lane quarters via smem.
-                float a[32];
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) a[jj] = v[jj] * v[jj];
-#pragma unroll
-                for (int w = 16; w >= 1; w >>= 1) {
-                    const bool up = (lane & w) != 0;
-#pragma unroll
-                    for (int jj = 0; jj < w; ++jj) {
-                        const float send = up ? a[jj] : a[jj + w];
-                        const float keep = up ? a[jj + w] : a[jj];
-                        a[jj] = keep + __shfl_xor_sync(0xffffffffu, send, w);
-                    }
-                }
-                red_s[quarter * 64 + 32 * half + lane] = a[0];
-                __syncthreads();
-                if (tid < CS) {
-                    const float ss = red_s[tid] + red_s[64 + tid] + red_s[128 + tid] + red_s[192 + tid];
-                    rstd_s[tid] = rsqrtf(ss / (float)HD + p.eps);
-                }
-                wait_bar(BAR_Z, ph);
-                __syncthreads();
-                const __nv_bfloat16* zt = reinterpret_cast<const __nv_bfloat16*>(smem + OFF_Z);
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int tok = 32 * half + jj;
-                    const float nb = bf16r(v[jj] * rstd_s[tok]);
-                    const float zf = __bfloat162float(zt[sw_off(tok, dv, 64) >> 1]);
-                    const float sg = zf * (1.f / (1.f + expf(-zf)));
-                    if (tok < valid) obase[(size_t)tok * ostride] = __float2bfloat16_rn((wgt * nb) * sg);
-                }
-            }
+            for (int jj = 0; jj < 32; ++jj) ot[sw_off(32 * half + jj, dv, 64) >> 1] = __float2bfloat16_rn(v[jj]);
         }
         ptx::tc_fence_before();
-        ptx::fence_proxy_async_smem();
+        ptx::fence_proxy_async_smem();  // S tiles
+        __syncthreads();
+
+        // ---- epilogue: 4 threads per token, 32 dv each, 16-byte accesses ----
+        {
+            float o[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t w4[4];
+                ld_shared_v4(sb + OFF_OST + sw_chunk(et, 4 * eq + c, 64), w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
+                    o[8 * c + 2 * u] = __bfloat162float(b2.x);
+                    o[8 * c + 2 * u + 1] = __bfloat162float(b2.y);
+                }
+            }
+            uint32_t outw[16];
+            if (!p.gated) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) outw[j] = pack_bf16(o[2 * j], o[2 * j + 1]);
+            } else {
+                float ss = 0.f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) ss = fmaf(o[j], o[j], ss);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                const float rstd = rsqrtf(ss * (1.f / (float)HD) + p.eps);
+                wait_bar(BAR_Z, ph);
+                float y[32];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w4[4];
+                    ld_shared_v4(sb + OFF_Z + sw_chunk(et, 4 * eq + c, 64), w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
+                        const float zz[2] = {__bfloat162float(b2.x), __bfloat162float(b2.y)};
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int j = 8 * c + 2 * u + e;
+                            const float nb = bf16r(o[j] * rstd);
+                            const float sg = zz[e] * rcpf(1.f + ex2f(-zz[e] * LOG2E));
+                            y[j] = (wgt[j] * nb) * sg;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) outw[j] = pack_bf16(y[2 * j], y[2 * j + 1]);
+            }
+            if (et < valid) {
+                uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + et) * p.HV * HD + (size_t)h * HD +
+                                                      32 * eq);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    dst[c] = make_uint4(outw[4 * c], outw[4 * c + 1], outw[4 * c + 2], outw[4 * c + 3]);
+            }
+        }
         __syncthreads();
         if (tid == 0 && p.gated && n + 1 < NC) {
             ptx::fence_proxy_async_smem();
@@ -813,7 +856,7 @@ static cudaError_t launch(const Launch& L) {
     const bool gated = (L.z != nullptr) || (L.w != nullptr);
     if (gated && (!L.z || !L.w)) return cudaErrorInvalidValue;
     if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || (gated && !aligned16(L.z)) ||
-        !aligned16(L.ws))
+        !aligned16(L.ws) || !aligned16(L.out))
         return cudaErrorInvalidValue;
     if (L.nseq == 0 || L.HV == 0) return cudaSuccess;
 

@@ -88,7 +88,7 @@ def test_stages_against_oracle_intermediates():
     errs["v_new"] = tensor_l2_rel(vnew, inter["v_new"])
     errs["o"] = tensor_l2_rel(of, inter["o"])
     print({k_: f"{v_:.3e}" for k_, v_ in errs.items()})
-    assert errs["c"] < 1e-5
+    assert errs["c"] < 1e-6 * max(1.0, float(np.abs(inter["c"]).max()))  # warp-scan vs sequential cumsum order
     assert errs["T"] < 1e-4
     assert errs["W"] < 1e-3
     assert errs["S_entry"] < 1e-3
