@@ -116,6 +116,27 @@ cudaError_t deltanet_chunk_prefill_varlen(
 cudaError_t gated_rmsnorm_forward(const void* o, const void* z, const void* w, void* y,
                                   int64_t rows, int dv, float eps, int dtype, cudaStream_t stream);
 
+/* No counterpart in the reference. For callers that cannot allocate device
+ * memory at call time (an inference engine's enqueue path that forbids
+ * cudaMalloc, a real-time loop where an allocation would synchronise the
+ * device): deltanet_chunk_prefill_gated with its scratch (the bounded-wait
+ * status word) in a static device array of at most 256 bytes held by every GPU
+ * that loads the library, instead of a workspace argument. Inputs and outputs
+ * are still the caller's. Allocates nothing. Returns cudaErrorInvalidValue if a
+ * call would need more scratch than the array holds. The first call on a device
+ * looks up the array's address (make it before any stream capture). All calls
+ * share the array and its last contents; calls that overlap on the GPU race on
+ * it. */
+cudaError_t deltanet_chunk_prefill_gated_noalloc(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    const void* z, const void* norm_w, float eps,
+    void* y,
+    const float* initial_state,
+    float* final_state,
+    int B, int T, int HV, int HQK, int DK, int DV, int chunk_size,
+    cudaStream_t stream);
+
 /* Copy the device status word of a workspace to *status_host (synchronises
  * `stream`). 0 = clean; bit 0 = a bounded wait timed out. Clears it when
  * clear != 0. No counterpart in the reference (its kernels have no waits). */

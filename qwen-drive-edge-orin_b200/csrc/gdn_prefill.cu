@@ -896,6 +896,34 @@ static cudaError_t launch(const Launch& L) {
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for callers that cannot allocate device memory (see
+// deltanet_chunk_prefill_gated_noalloc). A file-scope device array that every
+// GPU loading this library holds until exit; its host-side name is only a
+// stand-in, so the device address is looked up once per device with
+// cudaGetSymbolAddress while that device is current.
+constexpr size_t NOALLOC_SCRATCH_BYTES = 256;  // maximum scratch the no-alloc entry can serve
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+
+static cudaError_t noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[NOALLOC_MAX_DEVICES] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return cudaSuccess;
+}
+
 static size_t debug_bytes(int B, int T, int HV) {
     const size_t nc = (size_t)((T + CS - 1) / CS);
     return (size_t)B * HV * nc * DBG_REC * sizeof(float);
@@ -985,6 +1013,31 @@ cudaError_t deltanet_chunk_prefill_varlen(const void* q, const void* k, const vo
     L.max_nc = (T + gdn::CS - 1) / gdn::CS;
     L.ws = workspace; L.ws_bytes = workspace_bytes; L.stream = stream;
     return gdn::launch(L);
+}
+
+// Same computation as deltanet_chunk_prefill_gated, with its scratch (the
+// status word the bounded waits report to) taken from a static device array
+// instead of a caller-provided workspace, so the call performs no device
+// allocation at all (no cudaMalloc/cudaFree, no library allocator).
+// The first call on each device looks the array's address up, so make that
+// first call before any stream capture. Every call shares the one array:
+// calls whose kernels overlap on the GPU (concurrent streams) race on it; the
+// status word is cleared on `stream` before each launch.
+cudaError_t deltanet_chunk_prefill_gated_noalloc(const void* q, const void* k, const void* v,
+                                                 const float* g, const float* beta, const void* z,
+                                                 const void* norm_w, float eps, void* y,
+                                                 const float* initial_state, float* final_state,
+                                                 int B, int T, int HV, int HQK, int DK, int DV,
+                                                 int chunk_size, cudaStream_t stream) {
+    const size_t need = deltanet_prefill_workspace_size(B, T, HV, DK, DV, chunk_size);
+    if (need > gdn::NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;  // beyond the static maximum
+    void* ws = nullptr;
+    cudaError_t e = gdn::noalloc_scratch(&ws);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(ws, 0, need, stream);  // the status word must start at zero
+    if (e != cudaSuccess) return e;
+    return deltanet_chunk_prefill_gated(q, k, v, g, beta, z, norm_w, eps, y, initial_state, final_state, B, T,
+                                        HV, HQK, DK, DV, chunk_size, ws, gdn::NOALLOC_SCRATCH_BYTES, stream);
 }
 
 cudaError_t deltanet_read_status(void* workspace, int* status_host, int clear, cudaStream_t stream) {
