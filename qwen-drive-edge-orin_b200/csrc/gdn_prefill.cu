@@ -21,6 +21,9 @@
 // Precision: every operand that is not already a bf16 input (S, W, T', T'',
 // v_new, M) is split into bf16 hi + lo parts, so products keep ~16 mantissa
 // bits; accumulation is fp32 in TMEM; the state itself is fp32 in registers.
+// The per-chunk operands S^T and v_new^T are written by their owning threads
+// straight into TMEM and consumed there as the MMA A operand, which halves
+// the shared-memory traffic of those MMAs.
 // Exact bf16 inputs (q, k, v) enter the MMAs unscaled; per-token factors
 // (e^c, e^{c_L-c}) are applied in fp32 around them.
 //
@@ -55,45 +58,46 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t OFF_QK = 0;           // panel p: q rows 0-63 | k rows 64-127 (16 KB/panel)
 constexpr uint32_t OFF_V = 32768;        // v tile  [64 tok][128 dv]  (8 KB/panel)
 constexpr uint32_t OFF_Z = 49152;        // z tile  [64 tok][128 dv]
-constexpr uint32_t OFF_SHI = 65536;      // S^T hi  [128 dv][128 dk]  (16 KB/panel)
-constexpr uint32_t OFF_SLO = 98304;      // S^T lo
-constexpr uint32_t OFF_X = 131072;       // 64 KB exchange region (two phases)
+constexpr uint32_t OFF_X = 65536;        // 64 KB: T', T'' (hi/lo), W (hi/lo); inversion scratch
 constexpr uint32_t OFF_TP_HI = OFF_X + 0;       //  T'  = T diag(beta)        [64][64]
 constexpr uint32_t OFF_TP_LO = OFF_X + 8192;
 constexpr uint32_t OFF_TPP_HI = OFF_X + 16384;  //  T'' = T diag(beta e^c)    [64][64]
 constexpr uint32_t OFF_TPP_LO = OFF_X + 24576;
 constexpr uint32_t OFF_W_HI = OFF_X + 32768;    //  W   [64 tok][128 dk]  (8 KB/panel)
 constexpr uint32_t OFF_W_LO = OFF_X + 49152;
-constexpr uint32_t OFF_VN = OFF_X + 0;          //  v_new^T hi       [128 dv][64 tok]
-constexpr uint32_t OFF_VNP_HI = OFF_X + 16384;  //  (v_new e^{cL-c})^T hi
-constexpr uint32_t OFF_VNP_LO = OFF_X + 32768;  //                     lo
-constexpr uint32_t OFF_VN_LO = OFF_X + 49152;   //  v_new^T lo
-constexpr uint32_t OFF_XTMP = OFF_X + 0;        //  inversion scratch [3][16][16] fp32
-constexpr uint32_t OFF_L = 196608;       // L / T fp32 [64][65]; later M hi/lo
-constexpr uint32_t OFF_M_HI = OFF_L;     // M = scale (q k^T) * decay, [64][64] bf16
-constexpr uint32_t OFF_M_LO = OFF_L + 8192;
-constexpr uint32_t OFF_OST = OFF_L;      // o staging [64 tok][128 dv] bf16 after C3 (8 KB/panel)
-constexpr int LSTRIDE = 65;
-constexpr uint32_t OFF_MISC = OFF_L + 64 * LSTRIDE * 4;  // 213248
+constexpr uint32_t OFF_XTMP = OFF_X + 0;        //  inversion products P (fp32, 6 KB)
+constexpr uint32_t OFF_M_HI = 131072;    // M = scale (q k^T) * decay, [64][64] bf16
+constexpr uint32_t OFF_M_LO = 139264;
+constexpr uint32_t OFF_L = 147456;       // L / T fp32 [64][68]; o staging afterwards (8 KB/panel)
+constexpr uint32_t OFF_OST = OFF_L;
+constexpr int LSTRIDE = 68;              // 16-byte aligned rows for vector access
+constexpr uint32_t OFF_MISC = OFF_L + 64 * LSTRIDE * 4;  // 164864
 constexpr uint32_t MISC_C = 0;      // c        [64] f32
 constexpr uint32_t MISC_BETA = 256; // beta     [64]
 constexpr uint32_t MISC_EC = 512;   // e^c      [64]
 constexpr uint32_t MISC_ED = 768;   // e^{cL-c} [64]
-constexpr uint32_t MISC_BAR = 2304; // 6 mbarriers
-constexpr uint32_t MISC_TMEM = 2368;
-constexpr uint32_t MISC_FLAG = 2372;
-constexpr uint32_t MISC_BYTES = 2432;
+constexpr uint32_t MISC_BAR = 1024; // 5 mbarriers
+constexpr uint32_t MISC_TMEM = 1088;
+constexpr uint32_t MISC_FLAG = 1092;
+constexpr uint32_t MISC_BYTES = 1152;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
 constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;  // slack for manual 1024 alignment
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory limit");
 
-// TMEM columns of the accumulators (all 128 lanes).
-constexpr uint32_t TM_P = 0;     // [Q;K]K^T     64 cols
-constexpr uint32_t TM_V = 64;    // v_new^T      64 cols
-constexpr uint32_t TM_O = 128;   // S^T q^T      64 cols
-constexpr uint32_t TM_O2 = 192;  // v_new^T M^T  64 cols
-constexpr uint32_t TM_S = 256;   // dS^T        128 cols
-constexpr uint32_t TM_W = 384;   // W (M=64 layout: token rows in lanes 0-15 of each quarter), 128 cols
+// ---- TMEM map (columns; all 128 lanes). Regions are shared by operands
+// whose lifetimes do not overlap within a chunk.
+constexpr uint32_t TM_P = 0;       // P1 [Q;K]K^T fp32 (64)      -> then v_new^T hi/lo A operands
+constexpr uint32_t TM_VN_HI = 0;   //   v_new^T bf16 pairs (32)
+constexpr uint32_t TM_VN_LO = 32;
+constexpr uint32_t TM_V = 64;      // C12 v_new^T fp32 (64)      -> then (v_new e^{cL-c})^T hi/lo
+constexpr uint32_t TM_VP_HI = 64;
+constexpr uint32_t TM_VP_LO = 96;
+constexpr uint32_t TM_W = 128;     // P3 W fp32, M=64 layout (128) -> then C3 outputs
+constexpr uint32_t TM_O = 128;     //   S^T q^T (64)
+constexpr uint32_t TM_O2 = 192;    //   v_new^T M^T (64)
+constexpr uint32_t TM_S = 256;     // C4 dS^T fp32 (128)
+constexpr uint32_t TM_SA_HI = 384; // S^T bf16 pairs, A operand of C12 / C3 (64)
+constexpr uint32_t TM_SA_LO = 448;
 
 // Barrier slots.
 enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4 };
@@ -154,70 +158,6 @@ __device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_
                  : "r"(addr)
                  : "memory");
 }
-
-// Write 8 consecutive fp32 values as bf16 hi (and optionally lo) parts into a
-// 16-byte chunk of two tiles.
-__device__ __forceinline__ void put8_split(uint32_t hi_addr, uint32_t lo_addr, const float* x,
-                                           bool want_lo) {
-    float h[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = bf16r(x[i]);
-    st_shared_v4(hi_addr, pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]),
-                 pack_bf16(h[6], h[7]));
-    if (want_lo) {
-        st_shared_v4(lo_addr, pack_bf16(x[0] - h[0], x[1] - h[1]), pack_bf16(x[2] - h[2], x[3] - h[3]),
-                     pack_bf16(x[4] - h[4], x[5] - h[5]), pack_bf16(x[6] - h[6], x[7] - h[7]));
-    }
-}
-
-// T = (I + L)^-1 for a 64x64 strictly-lower L held in Ls (stride 65), in place.
-// 16x16 diagonal blocks by forward substitution (one warp each, lane = column,
-// column kept in registers); off-diagonal blocks by block rows:
-// T_rs = -T_rr * sum_{m=s}^{r-1} L_rm T_ms.
-__device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid) {
-    const int warp = tid >> 5, lane = tid & 31;
-    if (warp < 4 && lane < 16) {
-        const int b = warp, c = lane;
-        float t[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            float acc = (i == c) ? 1.f : 0.f;
-#pragma unroll
-            for (int j = 0; j < i; ++j) acc = fmaf(-Ls[(16 * b + i) * LSTRIDE + 16 * b + j], t[j], acc);
-            t[i] = acc;
-        }
-        __syncwarp(0x0000ffffu);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) Ls[(16 * b + i) * LSTRIDE + 16 * b + c] = t[i];
-    }
-    __syncthreads();
-#pragma unroll 1
-    for (int r = 1; r < 4; ++r) {
-        for (int e = tid; e < r * 256; e += NTHREADS) {
-            const int s = e >> 8, i = (e >> 4) & 15, c = e & 15;
-            float acc = 0.f;
-            for (int m = s; m < r; ++m) {
-                const float* lrow = Ls + (16 * r + i) * LSTRIDE + 16 * m;
-                const float* tcol = Ls + (16 * m) * LSTRIDE + 16 * s + c;
-#pragma unroll
-                for (int l = 0; l < 16; ++l) acc = fmaf(lrow[l], tcol[l * LSTRIDE], acc);
-            }
-            X[e] = acc;
-        }
-        __syncthreads();
-        for (int e = tid; e < r * 256; e += NTHREADS) {
-            const int s = e >> 8, i = (e >> 4) & 15, c = e & 15;
-            const float* trow = Ls + (16 * r + i) * LSTRIDE + 16 * r;
-            const float* xcol = X + s * 256 + c;
-            float acc = 0.f;
-#pragma unroll
-            for (int l = 0; l < 16; ++l) acc = fmaf(trow[l], xcol[l * 16], acc);
-            Ls[(16 * r + i) * LSTRIDE + 16 * s + c] = -acc;
-        }
-        __syncthreads();
-    }
-}
-
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -229,6 +169,136 @@ __device__ __forceinline__ float rcpf(float x) {
     return y;
 }
 constexpr float LOG2E = 1.4426950408889634f;
+
+// Split two fp32 values into packed bf16 hi parts and packed bf16 lo parts
+// (x = hi + lo to ~16 mantissa bits).
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_bf16(a - __low2float(h), b - __high2float(h));
+}
+
+// Write 8 consecutive fp32 values as bf16 hi (and optionally lo) parts into a
+// 16-byte chunk of two tiles.
+__device__ __forceinline__ void put8_split(uint32_t hi_addr, uint32_t lo_addr, const float* x,
+                                           bool want_lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) split2(x[2 * i], x[2 * i + 1], h[i], l[i]);
+    st_shared_v4(hi_addr, h[0], h[1], h[2], h[3]);
+    if (want_lo) st_shared_v4(lo_addr, l[0], l[1], l[2], l[3]);
+}
+
+// ---------------------------------------------------------------------------
+// T = (I + L)^-1 for a 64x64 strictly-lower L held in Ls (stride 68), in place.
+//   A: the four 16x16 diagonal blocks by forward substitution (one warp each,
+//      lane = column, column in registers);
+//   B/C: 32x32 halves: T_10 = -(T_11 L_10) T_00 and T_32 = -(T_33 L_32) T_22;
+//   D/E: T_[32:,:32] = -(T_[32:,32:] L_[32:,:32]) T_[:32,:32].
+// Every product is register-blocked 1x4 with 16-byte loads and uses the
+// triangular structure to skip zero terms. X holds the left products.
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
+    acc.x = fmaf(a, b.x, acc.x);
+    acc.y = fmaf(a, b.y, acc.y);
+    acc.z = fmaf(a, b.z, acc.z);
+    acc.w = fmaf(a, b.w, acc.w);
+}
+
+__device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    // A: diagonal blocks
+    if (warp < 4 && lane < 16) {
+        const int b = warp, c = lane;
+        const float* Lb = Ls + (16 * b) * LSTRIDE + 16 * b;
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float a0 = (i == c) ? 1.f : 0.f, a1 = 0.f;
+#pragma unroll
+            for (int j = 0; j + 1 < i; j += 2) {
+                a0 = fmaf(-Lb[i * LSTRIDE + j], t[j], a0);
+                a1 = fmaf(-Lb[i * LSTRIDE + j + 1], t[j + 1], a1);
+            }
+            if (i & 1) a0 = fmaf(-Lb[i * LSTRIDE + i - 1], t[i - 1], a0);
+            t[i] = a0 + a1;
+        }
+        __syncwarp(0x0000ffffu);
+        float* Tb = Ls + (16 * b) * LSTRIDE + 16 * b;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) Tb[i * LSTRIDE + c] = t[i];
+    }
+    __syncthreads();
+    // B: X[0:256] = T_11 L_10, X[256:512] = T_33 L_32   (16x16 each, stride 16).
+    // Terms above the diagonal of T_rr are stored zeros, so every unit runs the
+    // full 16-term range in groups of four with its loads issued together.
+    if (tid < 128) {
+        const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
+        const int r0 = 16 + 32 * blk, c0 = 32 * blk;  // T_rr at (r0, r0), L block at (r0, c0)
+        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+        const float* trow = Ls + (r0 + i) * LSTRIDE + r0;
+#pragma unroll
+        for (int m0 = 0; m0 < 16; m0 += 4) {
+            const float4 t4 = ld4(trow + m0);
+            const float4 b0 = ld4(Ls + (r0 + m0) * LSTRIDE + c0 + j0), b1 = ld4(Ls + (r0 + m0 + 1) * LSTRIDE + c0 + j0);
+            const float4 b2 = ld4(Ls + (r0 + m0 + 2) * LSTRIDE + c0 + j0), b3 = ld4(Ls + (r0 + m0 + 3) * LSTRIDE + c0 + j0);
+            fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
+        }
+        *reinterpret_cast<float4*>(X + blk * 256 + i * 16 + j0) =
+            make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
+    }
+    __syncthreads();
+    // C: T_10 = -X0 T_00 -> rows 16-31, cols 0-15; T_32 = -X1 T_22 -> rows 48-63, cols 32-47
+    if (tid < 128) {
+        const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
+        const int d0 = 32 * blk;  // T_ss at (d0, d0)
+        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+        const float* xrow = X + blk * 256 + i * 16;
+#pragma unroll
+        for (int m0 = 0; m0 < 16; m0 += 4) {
+            const float4 x4 = ld4(xrow + m0);
+            const float4 b0 = ld4(Ls + (d0 + m0) * LSTRIDE + d0 + j0), b1 = ld4(Ls + (d0 + m0 + 1) * LSTRIDE + d0 + j0);
+            const float4 b2 = ld4(Ls + (d0 + m0 + 2) * LSTRIDE + d0 + j0), b3 = ld4(Ls + (d0 + m0 + 3) * LSTRIDE + d0 + j0);
+            fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
+        }
+        *reinterpret_cast<float4*>(Ls + (d0 + 16 + i) * LSTRIDE + d0 + j0) =
+            make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
+    }
+    __syncthreads();
+    // D: X[512:1536] = T_[32:,32:] L_[32:,:32]   (32x32, stride 32)
+    {
+        const int i = tid >> 3, j0 = (tid & 7) * 4;
+        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+        const float* trow = Ls + (32 + i) * LSTRIDE + 32;
+        const int mend = (i + 4) & ~3;  // T_[32:,32:][i][m] = 0 for m > i
+#pragma unroll 2
+        for (int m0 = 0; m0 < mend; m0 += 4) {
+            const float4 t4 = ld4(trow + m0);
+            const float4 b0 = ld4(Ls + (32 + m0) * LSTRIDE + j0), b1 = ld4(Ls + (33 + m0) * LSTRIDE + j0);
+            const float4 b2 = ld4(Ls + (34 + m0) * LSTRIDE + j0), b3 = ld4(Ls + (35 + m0) * LSTRIDE + j0);
+            fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
+        }
+        *reinterpret_cast<float4*>(X + 512 + i * 32 + j0) =
+            make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
+    }
+    __syncthreads();
+    // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j)
+    {
+        const int i = tid >> 3, j0 = (tid & 7) * 4;
+        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+        const float* xrow = X + 512 + i * 32;
+#pragma unroll 2
+        for (int m0 = j0; m0 < 32; m0 += 4) {
+            const float4 x4 = ld4(xrow + m0);
+            const float4 b0 = ld4(Ls + m0 * LSTRIDE + j0), b1 = ld4(Ls + (m0 + 1) * LSTRIDE + j0);
+            const float4 b2 = ld4(Ls + (m0 + 2) * LSTRIDE + j0), b3 = ld4(Ls + (m0 + 3) * LSTRIDE + j0);
+            fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
+        }
+        *reinterpret_cast<float4*>(Ls + (32 + i) * LSTRIDE + j0) =
+            make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
+    }
+    __syncthreads();
+}
 
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -284,9 +354,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     ptx::tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC + MISC_TMEM);
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;  // this warp's TMEM lane quarter
+    const uint32_t tl = tmem + lane_addr;
 
-    // ---- initial state: thread (dv = row, dk in [64*half, 64*half+64)) ----
+    // S^T hi/lo (bf16 pairs) into TMEM as the A operand of C12 / C3:
+    // thread (dv = row, half) owns dk in [64*half, 64*half + 64) = 32 packed columns.
     float S[64];
+    auto store_state_operand = [&]() {
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) split2(S[32 * c2 + 2 * j], S[32 * c2 + 2 * j + 1], hi[j], lo[j]);
+            ptx::tmem_st16(tl + TM_SA_HI + 32 * half + 16 * c2, hi);
+            ptx::tmem_st16(tl + TM_SA_LO + 32 * half + 16 * c2, lo);
+        }
+    };
     {
         const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
 #pragma unroll
@@ -294,16 +376,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             const int dk = 64 * half + j;
             S[j] = (p.s0 != nullptr) ? __ldg(p.s0 + sbase + (size_t)dk * HD + row) : 0.f;
         }
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-            put8_split(sb + OFF_SHI + sw_chunk(row, 8 * half + ch, 128),
-                       sb + OFF_SLO + sw_chunk(row, 8 * half + ch, 128), S + 8 * ch, true);
+        store_state_operand();
     }
     // Epilogue mapping: token et = tid / 4, dv slice [32*eq, 32*eq + 32).
     const int et = tid >> 2, eq = tid & 3;
-    float wgt[32];
+    uint32_t wgt2[16];  // norm weight w[32*eq .. +32] as bf16 pairs
 #pragma unroll
-    for (int j = 0; j < 32; ++j) wgt[j] = p.gated ? __bfloat162float(p.w[32 * eq + j]) : 0.f;
+    for (int j = 0; j < 16; ++j)
+        wgt2[j] = p.gated ? *reinterpret_cast<const uint32_t*>(p.w + 32 * eq + 2 * j) : 0u;
 
     // ---- TMA issue helpers (thread 0) ----
     uint32_t issued[5] = {0, 0, 0, 0, 0}, consumed[5] = {0, 0, 0, 0, 0};
@@ -351,6 +431,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         wait_bar(BAR_MMA, consumed[BAR_MMA] & 1u);
         ptx::tc_fence_after();
     };
+    auto commit = [&]() {
+        ptx::mma_commit(bar(BAR_MMA));
+        ++issued[BAR_MMA];
+    };
 
     if (tid == 0 && NC > 0) {
         load_q(0);
@@ -374,22 +458,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         }
     };
     if (warp == 0 && NC > 0) load_gates(0);
-    ptx::fence_proxy_async_smem();  // S tiles written by all threads
+    ptx::tmem_wait_st();
+    ptx::tc_fence_before();
     __syncthreads();
 
-    // Instruction descriptors.
+    // Instruction descriptors (A operand from shared memory: *_SS; from TMEM: *_TS).
     constexpr uint32_t ID_P = ptx::idesc_bf16(128, 64, 0, 0, 0);    // [Q;K] K^T
     constexpr uint32_t ID_W = ptx::idesc_bf16(64, 128, 0, 1, 0);    // T'' K        (B MN-major)
     constexpr uint32_t ID_U = ptx::idesc_bf16(128, 64, 1, 0, 0);    // v^T T'^T     (A MN-major)
-    constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 64, 0, 0, 1);   // -S^T W^T
-    constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T q^T, v_new^T M^T
-    constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K   (B MN-major)
+    constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 64, 0, 0, 1);   // -S^T W^T     (A in TMEM)
+    constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T q^T, v_new^T M^T (A in TMEM)
+    constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K   (A in TMEM, B MN-major)
 
     for (int n = 0; n < NC; ++n) {
         if (*abort_flag) break;
         const int valid = min(CS, len - n * CS);
         const long long tok0 = tok_base + (long long)n * CS;
         const uint32_t ph = (uint32_t)(n & 1);
+        float* rec = p.dbg ? p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC : nullptr;
 
         // ---- gates: in-chunk inclusive cumsum of g (warp scan), decay factors ----
         if (warp == 0) {
@@ -425,23 +511,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint64_t b = ptx::sw128_desc(sb + OFF_QK + 8192 + koff, 16, 1024);
                 ptx::mma_bf16(tmem + TM_P, a, b, ID_P, s > 0);
             }
-            ptx::mma_commit(bar(BAR_MMA));
-            ++issued[BAR_MMA];
+            commit();
         }
         __syncthreads();  // c_s / beta_s visible
         wait_mma();
-        {
+        {   // rows 0-63: M = scale (q_i.k_j) e^{c_i-c_j}, j <= i (hi/lo); rows 64-127: L
             float v[32];
-            ptx::tmem_ld32(tmem + lane_addr + TM_P + 32 * half, v);
+            ptx::tmem_ld32(tl + TM_P + 32 * half, v);
             ptx::tmem_wait_ld();
-            // rows 0-63 (q.k) stay in TMEM until M is formed after C12
-            if (row >= CS) {  // L row i: beta_i k_i.k_j e^{c_i - c_j}, j < i
-                const int i = row - CS;
-                const float ci = c_s[i], bi = beta_s[i];
+            if (row < CS) {
+                const int i = row;
+                const float ci = c_s[i];
+                float m[32];
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) {
                     const int j = 32 * half + jj;
-                    Ls[i * LSTRIDE + j] = (j < i) ? bi * v[jj] * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                    m[jj] = (j <= i) ? v[jj] * p.scale * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                }
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    const uint32_t co = sw_chunk(i, 4 * half + ch, 64);
+                    put8_split(sb + OFF_M_HI + co, sb + OFF_M_LO + co, m + 8 * ch, true);
+                }
+            } else {  // L row i: beta_i k_i.k_j e^{c_i - c_j}, j < i
+                const int i = row - CS;
+                const float ci = c_s[i], bi = beta_s[i];
+                float* lrow = Ls + i * LSTRIDE + 32 * half;
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    float4 o4;
+                    float* o = reinterpret_cast<float*>(&o4);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int jj = 4 * j4 + u, j = 32 * half + jj;
+                        o[u] = (j < i) ? bi * v[jj] * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                    }
+                    *reinterpret_cast<float4*>(lrow + 4 * j4) = o4;
                 }
             }
         }
@@ -450,8 +555,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 
         // ---- T = (I + L)^-1 (fp32, CUDA cores) ----
         invert_unit_lower(Ls, X, tid);
-        if (p.dbg) {
-            float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
+        if (rec) {
             for (int e = tid; e < CS * CS; e += NTHREADS) rec[DBG_T + e] = Ls[(e >> 6) * LSTRIDE + (e & 63)];
             if (tid < CS) rec[DBG_C + tid] = c_s[tid];
         }
@@ -460,11 +564,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             const int i = tid >> 2, jb = tid & 3;
             float tp[16], tpp[16];
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-                const int j = 16 * jb + jj;
-                const float t = Ls[i * LSTRIDE + j];
-                tp[jj] = t * beta_s[j];
-                tpp[jj] = tp[jj] * ec_s[j];
+            for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 t4 = ld4(Ls + i * LSTRIDE + 16 * jb + 4 * q4);
+                const float tt[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int jj = 4 * q4 + u, j = 16 * jb + jj;
+                    tp[jj] = tt[u] * beta_s[j];
+                    tpp[jj] = tp[jj] * ec_s[j];
+                }
             }
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
@@ -489,15 +597,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                     ptx::mma_bf16(tmem + TM_W, a, b, ID_W, (part | s) > 0);
                 }
             }
-            ptx::mma_commit(bar(BAR_MMA));
-            ++issued[BAR_MMA];
+            commit();
         }
         wait_mma();
         {   // M=64 accumulator: token 16*quarter + lane (lanes 0-15), dk 64*half .. +63
 #pragma unroll
             for (int c2 = 0; c2 < 2; ++c2) {
                 float v[32];
-                ptx::tmem_ld32(tmem + lane_addr + TM_W + 64 * half + 32 * c2, v);
+                ptx::tmem_ld32(tl + TM_W + 64 * half + 32 * c2, v);
                 ptx::tmem_wait_ld();
                 if (lane < 16) {
                     const int tok = 16 * quarter + lane;
@@ -506,8 +613,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                         const uint32_t co = sw_chunk(tok, 8 * half + 4 * c2 + ch, 64);
                         put8_split(sb + OFF_W_HI + co, sb + OFF_W_LO + co, v + 8 * ch, true);
                     }
-                    if (p.dbg) {
-                        float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
+                    if (rec) {
 #pragma unroll
                         for (int jj = 0; jj < 32; ++jj) rec[DBG_W + tok * HD + 64 * half + 32 * c2 + jj] = v[jj];
                     }
@@ -523,7 +629,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         wait_bar(BAR_V, ph);
         if (tid == 0) {
             ptx::tc_fence_after();
-            bool first = true;
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
                 const uint32_t tp = part ? OFF_TP_LO : OFF_TP_HI;
@@ -531,70 +636,51 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 for (int s = 0; s < 4; ++s) {
                     const uint64_t a = ptx::sw128_desc(sb + OFF_V + s * 2048, 8192, 1024);
                     const uint64_t b = ptx::sw128_desc(sb + tp + s * 32, 16, 1024);
-                    ptx::mma_bf16(tmem + TM_V, a, b, ID_U, first ? 0u : 1u);
-                    first = false;
+                    ptx::mma_bf16(tmem + TM_V, a, b, ID_U, (part | s) > 0);
                 }
             }
-            // (S_hi, W_hi), (S_lo, W_hi), (S_hi, W_lo)
+            // (S_hi, W_hi), (S_lo, W_hi), (S_hi, W_lo); S^T from TMEM
 #pragma unroll
             for (int term = 0; term < 3; ++term) {
-                const uint32_t sa = (term == 1) ? OFF_SLO : OFF_SHI;
+                const uint32_t sa = (term == 1) ? TM_SA_LO : TM_SA_HI;
                 const uint32_t wb = (term == 2) ? OFF_W_LO : OFF_W_HI;
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
-                    const uint64_t a =
-                        ptx::sw128_desc(sb + sa + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
                     const uint64_t b = ptx::sw128_desc(sb + wb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024);
-                    ptx::mma_bf16(tmem + TM_V, a, b, ID_WS, 1u);
+                    ptx::mma_bf16_ts(tmem + TM_V, tmem + sa + 8 * s, b, ID_WS, 1u);
                 }
             }
-            ptx::mma_commit(bar(BAR_MMA));
-            ++issued[BAR_MMA];
+            commit();
         }
         wait_mma();
         if (tid == 0 && n + 1 < NC) load_v(n + 1);  // v tile consumed
-        {
+        {   // v_new^T (fp32, cols TM_V) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
-            ptx::tmem_ld32(tmem + lane_addr + TM_V + 32 * half, v);
+            ptx::tmem_ld32(tl + TM_V + 32 * half, v);
             ptx::tmem_wait_ld();
-            const int dv = row;
-            float vp[32];
+            if (rec) {
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) vp[jj] = v[jj] * ed_s[32 * half + jj];
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                const uint32_t co = sw_chunk(dv, 4 * half + ch, 128);
-                put8_split(sb + OFF_VN + co, sb + OFF_VN_LO + co, v + 8 * ch, true);
-                put8_split(sb + OFF_VNP_HI + co, sb + OFF_VNP_LO + co, vp + 8 * ch, true);
+                for (int jj = 0; jj < 32; ++jj) rec[DBG_VN + (32 * half + jj) * HD + row] = v[jj];
             }
-            if (p.dbg) {
-                float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
+            {   // v_new hi/lo -> cols [0, 64) (the consumed P1 accumulator)
+                uint32_t vh[16], vl[16];
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) rec[DBG_VN + (32 * half + jj) * HD + dv] = v[jj];
+                for (int j = 0; j < 16; ++j) split2(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
+                ptx::tmem_st16(tl + TM_VN_HI + 16 * half, vh);
+                ptx::tmem_st16(tl + TM_VN_LO + 16 * half, vl);
             }
-        }
-        {   // M row i: scale * (q_i.k_j) * e^{c_i - c_j} for j <= i, hi/lo, from the P1 accumulator
-            float v[32];
-            ptx::tmem_ld32(tmem + lane_addr + TM_P + 32 * half, v);
-            ptx::tmem_wait_ld();
-            if (row < CS) {
-                const int i = row;
-                const float ci = c_s[i];
-                float m[32];
+            uint32_t ph_[16], pl[16];
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int j = 32 * half + jj;
-                    m[jj] = (j <= i) ? v[jj] * p.scale * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
-                }
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    const uint32_t co = sw_chunk(i, 4 * half + ch, 64);
-                    put8_split(sb + OFF_M_HI + co, sb + OFF_M_LO + co, m + 8 * ch, true);
-                }
-            }
+            for (int j = 0; j < 16; ++j)
+                split2(v[2 * j] * ed_s[32 * half + 2 * j], v[2 * j + 1] * ed_s[32 * half + 2 * j + 1], ph_[j], pl[j]);
+            ptx::tc_fence_before();
+            __syncthreads();  // every thread has read TM_V before cols [64, 128) are overwritten
+            ptx::tc_fence_after();
+            ptx::tmem_st16(tl + TM_VP_HI + 16 * half, ph_);
+            ptx::tmem_st16(tl + TM_VP_LO + 16 * half, pl);
+            ptx::tmem_wait_st();
         }
         ptx::tc_fence_before();
-        ptx::fence_proxy_async_smem();
         __syncthreads();
         if (*abort_flag) break;
 
@@ -603,39 +689,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ptx::tc_fence_after();
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
-                const uint32_t sa = part ? OFF_SLO : OFF_SHI;
+                const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
-                    const uint64_t a =
-                        ptx::sw128_desc(sb + sa + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
                     const uint64_t b = ptx::sw128_desc(sb + OFF_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
-                    ptx::mma_bf16(tmem + TM_O, a, b, ID_O, (part | s) > 0);
+                    ptx::mma_bf16_ts(tmem + TM_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
                 }
             }
             // (VN_hi, M_hi), (VN_lo, M_hi), (VN_hi, M_lo)
 #pragma unroll
             for (int term = 0; term < 3; ++term) {
-                const uint32_t va = (term == 1) ? OFF_VN_LO : OFF_VN;
+                const uint32_t va = (term == 1) ? TM_VN_LO : TM_VN_HI;
                 const uint32_t mb = (term == 2) ? OFF_M_LO : OFF_M_HI;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const uint64_t a = ptx::sw128_desc(sb + va + s * 32, 16, 1024);
                     const uint64_t b = ptx::sw128_desc(sb + mb + s * 32, 16, 1024);
-                    ptx::mma_bf16(tmem + TM_O2, a, b, ID_O, (term | s) > 0);
+                    ptx::mma_bf16_ts(tmem + TM_O2, tmem + va + 8 * s, b, ID_O, (term | s) > 0);
                 }
             }
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
-                const uint32_t va = part ? OFF_VNP_LO : OFF_VNP_HI;
+                const uint32_t va = part ? TM_VP_LO : TM_VP_HI;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const uint64_t a = ptx::sw128_desc(sb + va + s * 32, 16, 1024);
                     const uint64_t b = ptx::sw128_desc(sb + OFF_QK + 8192 + s * 2048, 16384, 1024);
-                    ptx::mma_bf16(tmem + TM_S, a, b, ID_S, (part | s) > 0);
+                    ptx::mma_bf16_ts(tmem + TM_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
                 }
             }
-            ptx::mma_commit(bar(BAR_MMA));
-            ++issued[BAR_MMA];
+            commit();
         }
         wait_mma();
         if (tid == 0 && n + 1 < NC) {  // q and k tiles consumed
@@ -643,39 +724,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             load_k(n + 1);
         }
 
-        // ---- state update: S <- e^{cL} S + dS ----
+        // ---- state update: S <- e^{cL} S + dS; new S^T hi/lo into TMEM ----
         {
             const float gam = ec_s[CS - 1];
-            if (p.dbg) {
-                float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
+            if (rec) {
 #pragma unroll
                 for (int j = 0; j < 64; ++j) rec[DBG_SC + (64 * half + j) * HD + row] = S[j];
             }
 #pragma unroll
             for (int c2 = 0; c2 < 2; ++c2) {
                 float v[32];
-                ptx::tmem_ld32(tmem + lane_addr + TM_S + 64 * half + 32 * c2, v);
+                ptx::tmem_ld32(tl + TM_S + 64 * half + 32 * c2, v);
                 ptx::tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
             }
-#pragma unroll
-            for (int ch = 0; ch < 8; ++ch)
-                put8_split(sb + OFF_SHI + sw_chunk(row, 8 * half + ch, 128),
-                           sb + OFF_SLO + sw_chunk(row, 8 * half + ch, 128), S + 8 * ch, true);
         }
 
-        // ---- o = scale e^c o1 + o2, rounded to bf16, staged [tok][dv] (M tiles are dead) ----
+        // ---- o = scale e^c o1 + o2, rounded to bf16, staged [tok][dv] in the (free) L region ----
         {
             float v[32], v2[32];
-            ptx::tmem_ld32(tmem + lane_addr + TM_O + 32 * half, v);
-            ptx::tmem_ld32(tmem + lane_addr + TM_O2 + 32 * half, v2);
+            ptx::tmem_ld32(tl + TM_O + 32 * half, v);
+            ptx::tmem_ld32(tl + TM_O2 + 32 * half, v2);
             ptx::tmem_wait_ld();
             const int dv = row;
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) v[jj] = fmaf(p.scale * ec_s[32 * half + jj], v[jj], v2[jj]);
-            if (p.dbg) {
-                float* rec = p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC;
+            if (rec) {
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) rec[DBG_O + (32 * half + jj) * HD + dv] = v[jj];
             }
@@ -683,8 +758,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) ot[sw_off(32 * half + jj, dv, 64) >> 1] = __float2bfloat16_rn(v[jj]);
         }
+        store_state_operand();  // new S^T hi/lo for the next chunk's C12 / C3
+        ptx::tmem_wait_st();
         ptx::tc_fence_before();
-        ptx::fence_proxy_async_smem();  // S tiles
         __syncthreads();
 
         // ---- epilogue: 4 threads per token, 32 dv each, 16-byte accesses ----
@@ -713,26 +789,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 ss += __shfl_xor_sync(0xffffffffu, ss, 2);
                 const float rstd = rsqrtf(ss * (1.f / (float)HD) + p.eps);
                 wait_bar(BAR_Z, ph);
-                float y[32];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t w4[4];
                     ld_shared_v4(sb + OFF_Z + sw_chunk(et, 4 * eq + c, 64), w4[0], w4[1], w4[2], w4[3]);
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
-                        const float zz[2] = {__bfloat162float(b2.x), __bfloat162float(b2.y)};
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int j = 8 * c + 2 * u + e;
-                            const float nb = bf16r(o[j] * rstd);
-                            const float sg = zz[e] * rcpf(1.f + ex2f(-zz[e] * LOG2E));
-                            y[j] = (wgt[j] * nb) * sg;
-                        }
+                        const int j = 8 * c + 2 * u;  // elements j, j+1
+                        const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
+                        const __nv_bfloat162 w2 = *reinterpret_cast<const __nv_bfloat162*>(&wgt2[j >> 1]);
+                        const float z0 = __low2float(z2), z1 = __high2float(z2);
+                        const float y0 = (__low2float(w2) * bf16r(o[j] * rstd)) * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
+                        const float y1 =
+                            (__high2float(w2) * bf16r(o[j + 1] * rstd)) * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
+                        outw[j >> 1] = pack_bf16(y0, y1);
                     }
                 }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) outw[j] = pack_bf16(y[2 * j], y[2 * j + 1]);
             }
             if (et < valid) {
                 uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + et) * p.HV * HD + (size_t)h * HD +
@@ -761,6 +833,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     // Abort path: wait (bounded) for this CTA's own TMA copies and MMAs still
     // in flight before its shared memory and TMEM are released.
     if (*abort_flag && tid == 0) {
+#pragma unroll
         for (int i = 0; i < 5; ++i)
             while (consumed[i] < issued[i]) {
                 ptx::mbar_wait(bar(i), consumed[i] & 1u, WAIT_ITERS);
