@@ -63,15 +63,16 @@ constexpr uint32_t OFF_TP_HI = OFF_X + 0;       //  T'  = T diag(beta)        [6
 constexpr uint32_t OFF_TP_LO = OFF_X + 8192;
 constexpr uint32_t OFF_TPP_HI = OFF_X + 16384;  //  T'' = T diag(beta e^c)    [64][64]
 constexpr uint32_t OFF_TPP_LO = OFF_X + 24576;
-constexpr uint32_t OFF_W_HI = OFF_X + 32768;    //  W   [64 tok][128 dk]  (8 KB/panel)
-constexpr uint32_t OFF_W_LO = OFF_X + 49152;
+constexpr uint32_t OFF_W_HI = OFF_X + 32768;    //  W^T [128 dk][64 tok] (MN-major B operand)
+constexpr uint32_t OFF_W_LO = OFF_X + 49152;    //  (must follow W_HI by 16 KB: stacked along N)
 constexpr uint32_t OFF_XTMP = OFF_X + 0;        //  inversion products P (fp32, 6 KB)
 constexpr uint32_t OFF_M_HI = 131072;    // M = scale (q k^T) * decay, [64][64] bf16
 constexpr uint32_t OFF_M_LO = 139264;
 constexpr uint32_t OFF_L = 147456;       // L / T fp32 [64][68]; o staging afterwards (8 KB/panel)
 constexpr uint32_t OFF_OST = OFF_L;
 constexpr int LSTRIDE = 68;              // 16-byte aligned rows for vector access
-constexpr uint32_t OFF_MISC = OFF_L + 64 * LSTRIDE * 4;  // 164864
+constexpr uint32_t OFF_GATE = OFF_L + 64 * LSTRIDE * 4;  // 164864: w * silu(z), fp32 [64][128], 16-B chunks swizzled
+constexpr uint32_t OFF_MISC = OFF_GATE + 32768;          // 197632
 constexpr uint32_t MISC_C = 0;      // c        [64] f32
 constexpr uint32_t MISC_BETA = 256; // beta     [64]
 constexpr uint32_t MISC_EC = 512;   // e^c      [64]
@@ -79,7 +80,8 @@ constexpr uint32_t MISC_ED = 768;   // e^{cL-c} [64]
 constexpr uint32_t MISC_BAR = 1024; // 5 mbarriers
 constexpr uint32_t MISC_TMEM = 1088;
 constexpr uint32_t MISC_FLAG = 1092;
-constexpr uint32_t MISC_BYTES = 1152;
+constexpr uint32_t MISC_W = 1152;   // norm weight [128] f32
+constexpr uint32_t MISC_BYTES = 1664;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
 constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;  // slack for manual 1024 alignment
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory limit");
@@ -89,12 +91,12 @@ static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory 
 constexpr uint32_t TM_P = 0;       // P1 [Q;K]K^T fp32 (64)      -> then v_new^T hi/lo A operands
 constexpr uint32_t TM_VN_HI = 0;   //   v_new^T bf16 pairs (32)
 constexpr uint32_t TM_VN_LO = 32;
-constexpr uint32_t TM_V = 64;      // C12 v_new^T fp32 (64)      -> then (v_new e^{cL-c})^T hi/lo
-constexpr uint32_t TM_VP_HI = 64;
+constexpr uint32_t TM_V = 64;      // C12 [hi-part | lo-part] v_new^T fp32 (128) -> then:
+constexpr uint32_t TM_VP_HI = 64;  //   (v_new e^{cL-c})^T hi/lo (64)
 constexpr uint32_t TM_VP_LO = 96;
-constexpr uint32_t TM_W = 128;     // P3 W fp32, M=64 layout (128) -> then C3 outputs
-constexpr uint32_t TM_O = 128;     //   S^T q^T (64)
-constexpr uint32_t TM_O2 = 192;    //   v_new^T M^T (64)
+constexpr uint32_t TM_W = 128;     // P3 [T''_hi | T''_lo] parts of W^T fp32 (128), read before C12
+constexpr uint32_t TM_O = 128;     // C3 S^T q^T (64)
+constexpr uint32_t TM_O2 = 192;    //    v_new^T M^T (64)
 constexpr uint32_t TM_S = 256;     // C4 dS^T fp32 (128)
 constexpr uint32_t TM_SA_HI = 384; // S^T bf16 pairs, A operand of C12 / C3 (64)
 constexpr uint32_t TM_SA_LO = 448;
@@ -132,6 +134,11 @@ struct Params {
 __device__ __forceinline__ uint32_t sw_off(int row, int col, int rows) {
     return (uint32_t)((col >> 6) * rows * 128 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) +
                       ((col & 7) << 1));
+}
+// Byte offset of fp32 element group [4j, 4j+4) of row `row` in the [64][128] fp32 gate
+// tile: the 16-byte chunk index is XOR-swizzled with the row inside each group of 8.
+__device__ __forceinline__ uint32_t gate_chunk(int row, int j) {
+    return (uint32_t)(row * 512 + (((j & ~7) | ((j ^ row) & 7)) << 4));
 }
 // Byte offset of the 16-byte chunk holding cols [8*ch, 8*ch+8) of `row`.
 __device__ __forceinline__ uint32_t sw_chunk(int row, int ch, int rows) {
@@ -205,8 +212,12 @@ __device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
     acc.w = fmaf(a, b.w, acc.w);
 }
 
-__device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid) {
+// `idle(phase)` runs on threads 128-255 during phases A, B and C (phase = 0, 1, 2),
+// which use only threads 0-127.
+template <typename Idle>
+__device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, Idle&& idle) {
     const int warp = tid >> 5, lane = tid & 31;
+    if (tid >= 128) idle(0);
     // A: diagonal blocks
     if (warp < 4 && lane < 16) {
         const int b = warp, c = lane;
@@ -232,6 +243,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid) 
     // B: X[0:256] = T_11 L_10, X[256:512] = T_33 L_32   (16x16 each, stride 16).
     // Terms above the diagonal of T_rr are stored zeros, so every unit runs the
     // full 16-term range in groups of four with its loads issued together.
+    if (tid >= 128) idle(1);
     if (tid < 128) {
         const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
         const int r0 = 16 + 32 * blk, c0 = 32 * blk;  // T_rr at (r0, r0), L block at (r0, c0)
@@ -249,6 +261,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid) 
     }
     __syncthreads();
     // C: T_10 = -X0 T_00 -> rows 16-31, cols 0-15; T_32 = -X1 T_22 -> rows 48-63, cols 32-47
+    if (tid >= 128) idle(2);
     if (tid < 128) {
         const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
         const int d0 = 32 * blk;  // T_ss at (d0, d0)
@@ -378,12 +391,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         }
         store_state_operand();
     }
-    // Epilogue mapping: token et = tid / 4, dv slice [32*eq, 32*eq + 32).
+    // Epilogue mapping: token et = tid / 4, 16-byte output chunks {eq, eq+4, eq+8, eq+12}.
     const int et = tid >> 2, eq = tid & 3;
-    uint32_t wgt2[16];  // norm weight w[32*eq .. +32] as bf16 pairs
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-        wgt2[j] = p.gated ? *reinterpret_cast<const uint32_t*>(p.w + 32 * eq + 2 * j) : 0u;
+    float* w_s = misc + MISC_W / 4;
+    if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;
 
     // ---- TMA issue helpers (thread 0) ----
     uint32_t issued[5] = {0, 0, 0, 0, 0}, consumed[5] = {0, 0, 0, 0, 0};
@@ -440,8 +451,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         load_q(0);
         load_k(0);
         load_v(0);
-        if (p.gated) load_z(0);
     }
+    if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)
     // Gates of the next chunk are prefetched into warp 0's registers (lane l: tokens 2l, 2l+1).
     float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
     auto load_gates = [&](int n) {
@@ -464,9 +475,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 
     // Instruction descriptors (A operand from shared memory: *_SS; from TMEM: *_TS).
     constexpr uint32_t ID_P = ptx::idesc_bf16(128, 64, 0, 0, 0);    // [Q;K] K^T
-    constexpr uint32_t ID_W = ptx::idesc_bf16(64, 128, 0, 1, 0);    // T'' K        (B MN-major)
-    constexpr uint32_t ID_U = ptx::idesc_bf16(128, 64, 1, 0, 0);    // v^T T'^T     (A MN-major)
-    constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 64, 0, 0, 1);   // -S^T W^T     (A in TMEM)
+    constexpr uint32_t ID_W = ptx::idesc_bf16(128, 128, 1, 0, 0);   // K^T [T''_hi; T''_lo]^T  (A MN-major)
+    constexpr uint32_t ID_U = ptx::idesc_bf16(128, 128, 1, 0, 0);   // v^T [T'_hi; T'_lo]^T    (A MN-major)
+    constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 128, 0, 1, 1);  // -S^T [W_hi^T | W_lo^T]  (A in TMEM, B MN-major)
     constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T q^T, v_new^T M^T (A in TMEM)
     constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K   (A in TMEM, B MN-major)
 
@@ -553,8 +564,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::tc_fence_before();
         __syncthreads();
 
-        // ---- T = (I + L)^-1 (fp32, CUDA cores) ----
-        invert_unit_lower(Ls, X, tid);
+        // ---- T = (I + L)^-1 (fp32, CUDA cores); meanwhile warps 4-7 form gate = w * silu(z) ----
+        auto gate_work = [&](int phase) {
+            if (!p.gated) return;
+            if (phase == 0) wait_bar(BAR_Z, ph);
+            const int tg = tid - 128;
+            const int r0 = (phase == 0) ? 0 : (phase == 1 ? 32 : 48), nr = (phase == 0) ? 32 : 16;
+            for (int u = tg; u < nr * 16; u += 128) {
+                const int r = r0 + (u >> 4), zc = u & 15;
+                uint32_t w4[4];
+                ld_shared_v4(sb + OFF_Z + sw_chunk(r, zc, 64), w4[0], w4[1], w4[2], w4[3]);
+                float gv[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
+                    const float z0 = __low2float(z2), z1 = __high2float(z2);
+                    gv[2 * e] = w_s[8 * zc + 2 * e] * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
+                    gv[2 * e + 1] = w_s[8 * zc + 2 * e + 1] * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
+                }
+                *reinterpret_cast<float4*>(smem + OFF_GATE + gate_chunk(r, 2 * zc)) =
+                    make_float4(gv[0], gv[1], gv[2], gv[3]);
+                *reinterpret_cast<float4*>(smem + OFF_GATE + gate_chunk(r, 2 * zc + 1)) =
+                    make_float4(gv[4], gv[5], gv[6], gv[7]);
+            }
+            if (phase == 2) {
+                asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 4-7 are done with the z tile
+                if (tid == 128 && n + 1 < NC) {
+                    ptx::fence_proxy_async_smem();
+                    load_z(n + 1);
+                }
+            }
+        };
+        invert_unit_lower(Ls, X, tid, gate_work);
         if (rec) {
             for (int e = tid; e < CS * CS; e += NTHREADS) rec[DBG_T + e] = Ls[(e >> 6) * LSTRIDE + (e & 63)];
             if (tid < CS) rec[DBG_C + tid] = c_s[tid];
@@ -584,40 +625,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::fence_proxy_async_smem();
         __syncthreads();
 
-        // ---- P3: W = T'' K (hi + lo), M = 64 tokens x N = 128 dk ----
+        // ---- P3: W^T = K^T [T''_hi; T''_lo]^T: cols 0-63 the hi part, 64-127 the lo part ----
         if (tid == 0) {
             ptx::tc_fence_after();
 #pragma unroll
-            for (int part = 0; part < 2; ++part) {
-                const uint32_t tpp = part ? OFF_TPP_LO : OFF_TPP_HI;
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint64_t a = ptx::sw128_desc(sb + tpp + s * 32, 16, 1024);
-                    const uint64_t b = ptx::sw128_desc(sb + OFF_QK + 8192 + s * 2048, 16384, 1024);
-                    ptx::mma_bf16(tmem + TM_W, a, b, ID_W, (part | s) > 0);
-                }
+            for (int s = 0; s < 4; ++s) {
+                const uint64_t a = ptx::sw128_desc(sb + OFF_QK + 8192 + s * 2048, 16384, 1024);
+                const uint64_t b = ptx::sw128_desc(sb + OFF_TPP_HI + s * 32, 16, 1024);  // 128 rows: hi then lo
+                ptx::mma_bf16(tmem + TM_W, a, b, ID_W, s > 0);
             }
             commit();
         }
         wait_mma();
-        {   // M=64 accumulator: token 16*quarter + lane (lanes 0-15), dk 64*half .. +63
+        {   // thread (dk = row, half): W^T[dk][tok] for tok in [32*half, +32), written as rows of W^T
+            float v[32], v2[32];
+            ptx::tmem_ld32(tl + TM_W + 32 * half, v);
+            ptx::tmem_ld32(tl + TM_W + 64 + 32 * half, v2);
+            ptx::tmem_wait_ld();
 #pragma unroll
-            for (int c2 = 0; c2 < 2; ++c2) {
-                float v[32];
-                ptx::tmem_ld32(tl + TM_W + 64 * half + 32 * c2, v);
-                ptx::tmem_wait_ld();
-                if (lane < 16) {
-                    const int tok = 16 * quarter + lane;
+            for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
 #pragma unroll
-                    for (int ch = 0; ch < 4; ++ch) {
-                        const uint32_t co = sw_chunk(tok, 8 * half + 4 * c2 + ch, 64);
-                        put8_split(sb + OFF_W_HI + co, sb + OFF_W_LO + co, v + 8 * ch, true);
-                    }
-                    if (rec) {
+            for (int ch = 0; ch < 4; ++ch) {
+                const uint32_t co = sw_chunk(row, 4 * half + ch, 128);
+                put8_split(sb + OFF_W_HI + co, sb + OFF_W_LO + co, v + 8 * ch, true);
+            }
+            if (rec) {
 #pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) rec[DBG_W + tok * HD + 64 * half + 32 * c2 + jj] = v[jj];
-                    }
-                }
+                for (int jj = 0; jj < 32; ++jj) rec[DBG_W + (32 * half + jj) * HD + row] = v[jj];
             }
         }
         ptx::tc_fence_before();
@@ -629,24 +663,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         wait_bar(BAR_V, ph);
         if (tid == 0) {
             ptx::tc_fence_after();
+            // cols 0-63 accumulate the hi terms, cols 64-127 the lo terms (B stacked along N)
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const uint64_t a = ptx::sw128_desc(sb + OFF_V + s * 2048, 8192, 1024);
+                const uint64_t b = ptx::sw128_desc(sb + OFF_TP_HI + s * 32, 16, 1024);  // [T'_hi; T'_lo]
+                ptx::mma_bf16(tmem + TM_V, a, b, ID_U, s > 0);
+            }
+            // S_hi [W_hi | W_lo], S_lo [W_hi | W_lo]; S^T from TMEM, W^T tiles MN-major (LBO = 16 KB)
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
-                const uint32_t tp = part ? OFF_TP_LO : OFF_TP_HI;
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint64_t a = ptx::sw128_desc(sb + OFF_V + s * 2048, 8192, 1024);
-                    const uint64_t b = ptx::sw128_desc(sb + tp + s * 32, 16, 1024);
-                    ptx::mma_bf16(tmem + TM_V, a, b, ID_U, (part | s) > 0);
-                }
-            }
-            // (S_hi, W_hi), (S_lo, W_hi), (S_hi, W_lo); S^T from TMEM
-#pragma unroll
-            for (int term = 0; term < 3; ++term) {
-                const uint32_t sa = (term == 1) ? TM_SA_LO : TM_SA_HI;
-                const uint32_t wb = (term == 2) ? OFF_W_LO : OFF_W_HI;
+                const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
-                    const uint64_t b = ptx::sw128_desc(sb + wb + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024);
+                    const uint64_t b = ptx::sw128_desc(sb + OFF_W_HI + s * 2048, 16384, 1024);
                     ptx::mma_bf16_ts(tmem + TM_V, tmem + sa + 8 * s, b, ID_WS, 1u);
                 }
             }
@@ -656,8 +686,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         if (tid == 0 && n + 1 < NC) load_v(n + 1);  // v tile consumed
         {   // v_new^T (fp32, cols TM_V) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
-            ptx::tmem_ld32(tl + TM_V + 32 * half, v);
-            ptx::tmem_wait_ld();
+            {
+                float v2[32];
+                ptx::tmem_ld32(tl + TM_V + 32 * half, v);
+                ptx::tmem_ld32(tl + TM_V + 64 + 32 * half, v2);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
+            }
             if (rec) {
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) rec[DBG_VN + (32 * half + jj) * HD + row] = v[jj];
@@ -674,7 +710,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             for (int j = 0; j < 16; ++j)
                 split2(v[2 * j] * ed_s[32 * half + 2 * j], v[2 * j + 1] * ed_s[32 * half + 2 * j + 1], ph_[j], pl[j]);
             ptx::tc_fence_before();
-            __syncthreads();  // every thread has read TM_V before cols [64, 128) are overwritten
+            __syncthreads();  // every thread has read TM_V before cols [64, 192) are reused
             ptx::tc_fence_after();
             ptx::tmem_st16(tl + TM_VP_HI + 16 * half, ph_);
             ptx::tmem_st16(tl + TM_VP_LO + 16 * half, pl);
@@ -763,18 +799,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::tc_fence_before();
         __syncthreads();
 
-        // ---- epilogue: 4 threads per token, 32 dv each, 16-byte accesses ----
+        // ---- epilogue: 4 threads per token, 16-byte chunks {eq, eq+4, eq+8, eq+12} ----
         {
             float o[32];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int m = 0; m < 4; ++m) {
                 uint32_t w4[4];
-                ld_shared_v4(sb + OFF_OST + sw_chunk(et, 4 * eq + c, 64), w4[0], w4[1], w4[2], w4[3]);
+                ld_shared_v4(sb + OFF_OST + sw_chunk(et, eq + 4 * m, 64), w4[0], w4[1], w4[2], w4[3]);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
-                    o[8 * c + 2 * u] = __bfloat162float(b2.x);
-                    o[8 * c + 2 * u + 1] = __bfloat162float(b2.y);
+                    o[8 * m + 2 * u] = __bfloat162float(b2.x);
+                    o[8 * m + 2 * u + 1] = __bfloat162float(b2.y);
                 }
             }
             uint32_t outw[16];
@@ -788,37 +824,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 ss += __shfl_xor_sync(0xffffffffu, ss, 1);
                 ss += __shfl_xor_sync(0xffffffffu, ss, 2);
                 const float rstd = rsqrtf(ss * (1.f / (float)HD) + p.eps);
-                wait_bar(BAR_Z, ph);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t w4[4];
-                    ld_shared_v4(sb + OFF_Z + sw_chunk(et, 4 * eq + c, 64), w4[0], w4[1], w4[2], w4[3]);
+                for (int m = 0; m < 4; ++m) {
+                    const int c = eq + 4 * m;
+                    const float4 g0 = *reinterpret_cast<const float4*>(smem + OFF_GATE + gate_chunk(et, 2 * c));
+                    const float4 g1 = *reinterpret_cast<const float4*>(smem + OFF_GATE + gate_chunk(et, 2 * c + 1));
+                    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int j = 8 * c + 2 * u;  // elements j, j+1
-                        const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
-                        const __nv_bfloat162 w2 = *reinterpret_cast<const __nv_bfloat162*>(&wgt2[j >> 1]);
-                        const float z0 = __low2float(z2), z1 = __high2float(z2);
-                        const float y0 = (__low2float(w2) * bf16r(o[j] * rstd)) * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
-                        const float y1 =
-                            (__high2float(w2) * bf16r(o[j + 1] * rstd)) * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
-                        outw[j >> 1] = pack_bf16(y0, y1);
-                    }
+                    for (int e = 0; e < 4; ++e)
+                        outw[4 * m + e] = pack_bf16(bf16r(o[8 * m + 2 * e] * rstd) * gg[2 * e],
+                                                    bf16r(o[8 * m + 2 * e + 1] * rstd) * gg[2 * e + 1]);
                 }
             }
             if (et < valid) {
-                uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + et) * p.HV * HD + (size_t)h * HD +
-                                                      32 * eq);
+                uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + et) * p.HV * HD + (size_t)h * HD);
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    dst[c] = make_uint4(outw[4 * c], outw[4 * c + 1], outw[4 * c + 2], outw[4 * c + 3]);
+                for (int m = 0; m < 4; ++m)
+                    dst[eq + 4 * m] = make_uint4(outw[4 * m], outw[4 * m + 1], outw[4 * m + 2], outw[4 * m + 3]);
             }
         }
         __syncthreads();
-        if (tid == 0 && p.gated && n + 1 < NC) {
-            ptx::fence_proxy_async_smem();
-            load_z(n + 1);  // z tile consumed
-        }
     }
 
     // ---- final state ----
@@ -832,7 +857,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     }
     // Abort path: wait (bounded) for this CTA's own TMA copies and MMAs still
     // in flight before its shared memory and TMEM are released.
-    if (*abort_flag && tid == 0) {
+    if (*abort_flag && (tid == 0 || tid == 128)) {
 #pragma unroll
         for (int i = 0; i < 5; ++i)
             while (consumed[i] < issued[i]) {
