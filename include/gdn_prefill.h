@@ -109,6 +109,37 @@ cudaError_t deltanet_chunk_prefill_varlen(
     void* workspace, size_t workspace_bytes,
     cudaStream_t stream);
 
+/* Inputs of the reference's TRT prefill adapter: the GDNParams fields that
+ * runGdnChunkPrefillSm87 reads (gdnChunkPrefillSm87.cu:188-230), plus an
+ * optional fused gated RMSNorm and the workspace. */
+typedef struct gdn_prefill_params {
+    const void* q;        /* fp16 [n, seq_len, h, k_dim], not normalised */
+    const void* k;        /* fp16 [n, seq_len, h, k_dim], not normalised */
+    const void* v;        /* fp16 [n, seq_len, hv, v_dim] */
+    const void* a;        /* fp16 [n, seq_len, hv]  (decay pre-activation) */
+    const void* b;        /* fp16 [n, seq_len, hv]  (beta pre-activation) */
+    const float* A_log;   /* fp32 [hv] */
+    const void* dt_bias;  /* fp16 [hv] */
+    float* h0_source;     /* fp32 [n, hv, k_dim, v_dim]: initial state in, final state out (in place) */
+    void* o;              /* fp16 [n, seq_len, hv, v_dim] out (y when z and norm_w are set) */
+    const void* z;        /* optional fp16 [n, seq_len, hv, v_dim]: fuse the gated RMSNorm */
+    const void* norm_w;   /* optional fp16 [v_dim] */
+    float eps;            /* norm epsilon (used with z) */
+    int n, seq_len, h, hv, k_dim, v_dim;
+    void* workspace;      /* >= deltanet_prefill_workspace_size(...) bytes, device memory */
+    size_t workspace_bytes;
+} gdn_prefill_params;
+
+/* One GDN prefill with the adapter's pre-stage fused into the kernel's load
+ * path: q/k L2-normalised in fp32 (eps 1e-6) and rounded to bf16, v rounded to
+ * bf16, g = -exp(A_log) * softplus(a + dt_bias) and beta = sigmoid(b) in fp32,
+ * output o rounded to bf16 then stored as fp16, final state written back into
+ * h0_source. Replaces runGdnChunkPrefillSm87 (gdnChunkPrefillSm87.h:21) and its
+ * four pre-stage / conversion kernels and state copy-back
+ * (gdnChunkPrefillSm87.cu:44-125, 246-313) with one launch. Returns 0 on
+ * success, -1 (with a message on stderr) on failure, as the reference. */
+int gdn_run_chunk_prefill(const gdn_prefill_params* params, cudaStream_t stream);
+
 /* Standalone gated RMSNorm over rows of dv: y = w * round(o * rsqrt(mean(o^2)+eps)) * silu(z).
  * dtype 0 = fp16 I/O (the reference plugin's only format,
  * gatedRmsNormPlugin.cpp:155-167), 1 = bf16 I/O. Replaces

@@ -38,6 +38,8 @@ __all__ = [
     "recurrent_gated_delta_rule",
     "gdn_gate",
     "softplus",
+    "fp16_round",
+    "adapter_prefill",
 ]
 
 
@@ -234,7 +236,12 @@ def chunk_gated_delta_rule_varlen(q, k, v, g, beta, cu_seqlens, chunk_size: int 
     return o, states
 
 
-def gated_rmsnorm(o, z, w, eps: float = 1e-6):
+def fp16_round(x: np.ndarray) -> np.ndarray:
+    """Round float32 values to float16 (nearest, ties to even), returned as float32."""
+    return np.asarray(x, np.float32).astype(np.float16).astype(np.float32)
+
+
+def gated_rmsnorm(o, z, w, eps: float = 1e-6, io_dtype: str = "bf16"):
     """y = bf16( (w * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z) ), float32 math, rows over the last dim.
 
     Follows ``gatedRmsNormKernel.cu:21-54``: sum of squares in fp32 (:33-41),
@@ -243,13 +250,31 @@ def gated_rmsnorm(o, z, w, eps: float = 1e-6):
     With bf16 I/O this is ``Qwen3_5RMSNormGated.forward`` with a float32 weight
     holding the bf16 values (transformers ``modeling_qwen3_5.py:181-190``).
     """
+    rnd = bf16_round if io_dtype == "bf16" else fp16_round
     o = np.asarray(o, np.float32)
     z = np.asarray(z, np.float32)
     w = np.asarray(w, np.float32)
     var = (o * o).mean(axis=-1, keepdims=True, dtype=np.float32)
-    n = bf16_round(o * (1.0 / np.sqrt(var + np.float32(eps))).astype(np.float32))
+    n = rnd(o * (1.0 / np.sqrt(var + np.float32(eps))).astype(np.float32))
     silu = (z / (1.0 + np.exp(-z))).astype(np.float32)
-    return bf16_round((w * n) * silu)
+    return rnd((w * n) * silu)
+
+
+def adapter_prefill(q16, k16, v16, a16, b16, A_log, dt_bias16, h0, z16=None, w16=None, eps: float = 1e-6):
+    """The reference's TRT adapter composition (gdnChunkPrefillSm87.cu:186-320): q/k L2-normalised in
+    fp32 and rounded to bf16 (:52-85), v rounded to bf16 (:88-98), gates in fp32 (:113-125), the chunked
+    rule with h0 as the initial state, o rounded to bf16 then converted to fp16 (:100-110, :300).
+    With z/w, the fp16 gated RMSNorm of the plugin follows (gatedRmsNormKernel.cu:21-54).
+    Returns (o or y as fp16-valued float32, final state fp32)."""
+    q = bf16_round(l2norm(np.asarray(q16, np.float32)))
+    k = bf16_round(l2norm(np.asarray(k16, np.float32)))
+    v = bf16_round(np.asarray(v16, np.float32))
+    g, beta = gdn_gate(a16, b16, A_log, dt_bias16)
+    o, sf = chunk_gated_delta_rule(q, k, v, g, beta, 64, h0)
+    o16 = fp16_round(o)
+    if z16 is not None:
+        return gated_rmsnorm(o16, z16, w16, eps, io_dtype="fp16"), sf
+    return o16, sf
 
 
 def recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None):

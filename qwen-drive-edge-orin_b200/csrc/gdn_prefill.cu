@@ -36,6 +36,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <string.h>
 
 #include <atomic>
@@ -127,6 +128,15 @@ struct Params {
     float scale;                   // 1/sqrt(DK)
     float eps;
     int gated;
+    // Pre-stage mode (the reference's TRT adapter inputs): q/k/v/z/w and the
+    // output are fp16, q/k arrive un-normalised (L2-normalised here in fp32 and
+    // rounded to bf16), v is rounded to bf16, and the gates are computed from
+    // a, b (fp16 [.., HV]), A_log (fp32 [HV]) and dt_bias (fp16 [HV]).
+    int prestage;
+    const __half* ga;
+    const __half* gb;
+    const float* A_log;
+    const __half* dt_bias;
 };
 
 // Byte offset of bf16 element (row, col) in a 128B-swizzled tile whose panels
@@ -387,14 +397,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
         for (int j = 0; j < 64; ++j) {
             const int dk = 64 * half + j;
-            S[j] = (p.s0 != nullptr) ? __ldg(p.s0 + sbase + (size_t)dk * HD + row) : 0.f;
+            // plain load: the adapter passes the same buffer as s0 and sf (read here, written at exit)
+            S[j] = (p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f;
         }
         store_state_operand();
     }
     // Epilogue mapping: token et = tid / 4, 16-byte output chunks {eq, eq+4, eq+8, eq+12}.
     const int et = tid >> 2, eq = tid & 3;
     float* w_s = misc + MISC_W / 4;
-    if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;
+    if (tid < HD)
+        w_s[tid] = !p.gated ? 0.f
+                   : (p.prestage ? __half2float(reinterpret_cast<const __half*>(p.w)[tid]) : __bfloat162float(p.w[tid]));
 
     // ---- TMA issue helpers (thread 0) ----
     uint32_t issued[5] = {0, 0, 0, 0, 0}, consumed[5] = {0, 0, 0, 0, 0};
@@ -455,18 +468,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)
     // Gates of the next chunk are prefetched into warp 0's registers (lane l: tokens 2l, 2l+1).
     float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
+    // Pre-stage gate math (gdnChunkPrefillSm87.cu:44-49, 113-125):
+    // g = -exp(A_log[h]) * softplus(a + dt_bias[h]) (threshold 20), beta = sigmoid(b).
+    const float gA = p.prestage ? -expf(__ldg(p.A_log + h)) : 0.f;
+    const float gdt = p.prestage ? __half2float(p.dt_bias[h]) : 0.f;
+    auto gate_of = [&](size_t i, float& gv, float& bv) {
+        if (p.prestage) {
+            const float x = __half2float(p.ga[i]) + gdt;
+            gv = gA * (x > 20.f ? x : log1pf(expf(x)));
+            bv = 1.f / (1.f + expf(-__half2float(p.gb[i])));
+        } else {
+            gv = __ldg(p.g + i);
+            bv = __ldg(p.beta + i);
+        }
+    };
     auto load_gates = [&](int n) {
         const int valid = min(CS, len - n * CS);
         const long long t0 = tok_base + (long long)n * CS;
         gn0 = gn1 = bn0 = bn1 = 0.f;
-        if (2 * lane < valid) {
-            gn0 = __ldg(p.g + (size_t)(t0 + 2 * lane) * p.HV + h);
-            bn0 = __ldg(p.beta + (size_t)(t0 + 2 * lane) * p.HV + h);
-        }
-        if (2 * lane + 1 < valid) {
-            gn1 = __ldg(p.g + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
-            bn1 = __ldg(p.beta + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
-        }
+        if (2 * lane < valid) gate_of((size_t)(t0 + 2 * lane) * p.HV + h, gn0, bn0);
+        if (2 * lane + 1 < valid) gate_of((size_t)(t0 + 2 * lane + 1) * p.HV + h, gn1, bn1);
     };
     if (warp == 0 && NC > 0) load_gates(0);
     ptx::tmem_wait_st();
@@ -513,6 +534,36 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         // ---- P1: [Q;K] K^T ----
         wait_bar(BAR_Q, ph);
         wait_bar(BAR_K, ph);
+        if (p.prestage) {
+            // fp16 q/k rows -> fp32 L2 normalisation (eps 1e-6 inside the rsqrt) -> bf16, in
+            // place; two threads per row (64 elements each), rows 0-63 q, 64-127 k.
+            const int r = tid >> 1, hf = tid & 1;
+            float x[64];
+            float ss = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t w4[4];
+                ld_shared_v4(sb + OFF_QK + sw_chunk(r, 8 * hf + c, 128), w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const __half2 h2 = *reinterpret_cast<const __half2*>(&w4[u]);
+                    x[8 * c + 2 * u] = __low2float(h2);
+                    x[8 * c + 2 * u + 1] = __high2float(h2);
+                    ss = fmaf(x[8 * c + 2 * u], x[8 * c + 2 * u], ss);
+                    ss = fmaf(x[8 * c + 2 * u + 1], x[8 * c + 2 * u + 1], ss);
+                }
+            }
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            const float inv = rsqrtf(ss + 1e-6f);
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                st_shared_v4(sb + OFF_QK + sw_chunk(r, 8 * hf + c, 128), pack_bf16(x[8 * c] * inv, x[8 * c + 1] * inv),
+                             pack_bf16(x[8 * c + 2] * inv, x[8 * c + 3] * inv),
+                             pack_bf16(x[8 * c + 4] * inv, x[8 * c + 5] * inv),
+                             pack_bf16(x[8 * c + 6] * inv, x[8 * c + 7] * inv));
+            ptx::fence_proxy_async_smem();
+            __syncthreads();
+        }
         if (tid == 0) {
             ptx::tc_fence_after();
 #pragma unroll
@@ -577,8 +628,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 float gv[8];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
-                    const float z0 = __low2float(z2), z1 = __high2float(z2);
+                    float z0, z1;
+                    if (p.prestage) {
+                        const __half2 z2 = *reinterpret_cast<const __half2*>(&w4[e]);
+                        z0 = __low2float(z2), z1 = __high2float(z2);
+                    } else {
+                        const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
+                        z0 = __low2float(z2), z1 = __high2float(z2);
+                    }
                     gv[2 * e] = w_s[8 * zc + 2 * e] * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
                     gv[2 * e + 1] = w_s[8 * zc + 2 * e + 1] * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
                 }
@@ -661,6 +718,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 
         // ---- C12: v_new^T = v^T T'^T - S^T W^T ----
         wait_bar(BAR_V, ph);
+        if (p.prestage) {  // fp16 v -> bf16 in place (gdnChunkPrefillSm87.cu:88-98)
+#pragma unroll
+            for (int e = tid; e < 1024; e += NTHREADS) {
+                uint32_t w4[4];
+                const uint32_t a = sb + OFF_V + (uint32_t)e * 16;
+                ld_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const __half2 h2 = *reinterpret_cast<const __half2*>(&w4[u]);
+                    w4[u] = pack_bf16(__low2float(h2), __high2float(h2));
+                }
+                st_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
+            }
+            ptx::fence_proxy_async_smem();
+            __syncthreads();
+        }
         if (tid == 0) {
             ptx::tc_fence_after();
             // cols 0-63 accumulate the hi terms, cols 64-127 the lo terms (B stacked along N)
@@ -814,10 +887,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
             }
             uint32_t outw[16];
+            // Output rounding: bf16, or in pre-stage mode fp16 (o is already a bf16 value,
+            // exactly representable in fp16 inside its range, as the adapter's bf16->fp16 bridge).
+            auto pack_out = [&](float a, float b) -> uint32_t {
+                if (p.prestage) {
+                    const __half2 h2 = __floats2half2_rn(a, b);
+                    return *reinterpret_cast<const uint32_t*>(&h2);
+                }
+                return pack_bf16(a, b);
+            };
+            auto round_in = [&](float x) -> float {  // the norm's round-to-input-dtype step
+                return p.prestage ? __half2float(__float2half_rn(x)) : bf16r(x);
+            };
             if (!p.gated) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) outw[j] = pack_bf16(o[2 * j], o[2 * j + 1]);
+                for (int j = 0; j < 16; ++j) outw[j] = pack_out(o[2 * j], o[2 * j + 1]);
             } else {
+                if (p.prestage) {  // the norm reads the adapter's fp16 o (bf16 -> fp16 bridge, subnormals included)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] = __half2float(__float2half_rn(o[j]));
+                }
                 float ss = 0.f;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) ss = fmaf(o[j], o[j], ss);
@@ -832,8 +921,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                     const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
-                        outw[4 * m + e] = pack_bf16(bf16r(o[8 * m + 2 * e] * rstd) * gg[2 * e],
-                                                    bf16r(o[8 * m + 2 * e + 1] * rstd) * gg[2 * e + 1]);
+                        outw[4 * m + e] = pack_out(round_in(o[8 * m + 2 * e] * rstd) * gg[2 * e],
+                                                   round_in(o[8 * m + 2 * e + 1] * rstd) * gg[2 * e + 1]);
                 }
             }
             if (et < valid) {
@@ -897,14 +986,15 @@ static EncodeTiledFn get_encode_fn() {
 
 // 4-D bf16 tensor map over [B][T][H][128] (inner -> outer: dim, head, token, batch),
 // box 64 x 1 x 64 x 1 with 128-byte swizzle; out-of-bounds rows read as zero.
-static bool make_map(CUtensorMap* m, const void* base, int H, int T, int B) {
+static bool make_map(CUtensorMap* m, const void* base, int H, int T, int B, bool fp16 = false) {
     EncodeTiledFn enc = get_encode_fn();
     if (!enc) return false;
     cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
     cuuint64_t strides[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)T * H * HD * 2};
     cuuint32_t box[4] = {64, 1, 64, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+    CUresult r = enc(m, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                     const_cast<void*>(base), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -942,14 +1032,18 @@ struct Launch {
     size_t ws_bytes;
     float* dbg;
     cudaStream_t stream;
+    // pre-stage (adapter) inputs
+    int prestage;
+    const void *ga, *gb, *dt_bias;
+    const float* A_log;
 };
 
 static cudaError_t launch(const Launch& L) {
     if (L.DK != HD || L.DV != HD || L.chunk != CS) return cudaErrorInvalidValue;
     if (L.HQK <= 0 || L.HV <= 0 || L.HV % L.HQK != 0) return cudaErrorInvalidValue;
     if (L.T < 0 || L.nseq < 0 || L.HV > 65535 || L.nseq > 65535) return cudaErrorInvalidValue;
-    if (!L.q || !L.k || !L.v || !L.g || !L.beta || !L.out || !L.sf || !L.ws)
-        return cudaErrorInvalidValue;
+    if (!L.q || !L.k || !L.v || !L.out || !L.sf || !L.ws) return cudaErrorInvalidValue;
+    if (L.prestage ? (!L.ga || !L.gb || !L.A_log || !L.dt_bias) : (!L.g || !L.beta)) return cudaErrorInvalidValue;
     if (L.ws_bytes < WS_HEADER) return cudaErrorInvalidValue;
     const bool gated = (L.z != nullptr) || (L.w != nullptr);
     if (gated && (!L.z || !L.w)) return cudaErrorInvalidValue;
@@ -962,11 +1056,12 @@ static cudaError_t launch(const Launch& L) {
     memset(&p, 0, sizeof(p));
     const int Bmap = L.cu ? 1 : L.B;
     const int Tmap = L.T > 0 ? L.T : 1;
-    if (!make_map(&p.tm_q, L.q, L.HQK, Tmap, Bmap) || !make_map(&p.tm_k, L.k, L.HQK, Tmap, Bmap) ||
-        !make_map(&p.tm_v, L.v, L.HV, Tmap, Bmap))
+    const bool f16 = L.prestage != 0;
+    if (!make_map(&p.tm_q, L.q, L.HQK, Tmap, Bmap, f16) || !make_map(&p.tm_k, L.k, L.HQK, Tmap, Bmap, f16) ||
+        !make_map(&p.tm_v, L.v, L.HV, Tmap, Bmap, f16))
         return cudaErrorInvalidValue;
     if (gated) {
-        if (!make_map(&p.tm_z, L.z, L.HV, Tmap, Bmap)) return cudaErrorInvalidValue;
+        if (!make_map(&p.tm_z, L.z, L.HV, Tmap, Bmap, f16)) return cudaErrorInvalidValue;
     } else {
         p.tm_z = p.tm_v;
     }
@@ -986,6 +1081,11 @@ static cudaError_t launch(const Launch& L) {
     p.scale = 1.0f / sqrtf((float)L.DK);
     p.eps = L.eps;
     p.gated = gated ? 1 : 0;
+    p.prestage = L.prestage;
+    p.ga = static_cast<const __half*>(L.ga);
+    p.gb = static_cast<const __half*>(L.gb);
+    p.A_log = L.A_log;
+    p.dt_bias = static_cast<const __half*>(L.dt_bias);
 
     cudaError_t e = ensure_smem_attr();
     if (e != cudaSuccess) return e;
@@ -1136,6 +1236,49 @@ cudaError_t deltanet_chunk_prefill_gated_noalloc(const void* q, const void* k, c
     if (e != cudaSuccess) return e;
     return deltanet_chunk_prefill_gated(q, k, v, g, beta, z, norm_w, eps, y, initial_state, final_state, B, T,
                                         HV, HQK, DK, DV, chunk_size, ws, gdn::NOALLOC_SCRATCH_BYTES, stream);
+}
+
+int gdn_run_chunk_prefill(const gdn_prefill_params* params, cudaStream_t stream) {
+    if (params == nullptr) {
+        fprintf(stderr, "gdn_run_chunk_prefill: null params\n");
+        return -1;
+    }
+    const gdn_prefill_params& P = *params;
+    if (P.k_dim != gdn::HD || P.v_dim != gdn::HD) {
+        fprintf(stderr, "gdn_run_chunk_prefill: requires k_dim=v_dim=128, got %d/%d\n", P.k_dim, P.v_dim);
+        return -1;
+    }
+    if (P.h <= 0 || P.hv <= 0 || P.hv < P.h || P.hv % P.h != 0) {
+        fprintf(stderr, "gdn_run_chunk_prefill: requires hv >= h and hv %% h == 0, got h=%d hv=%d\n", P.h, P.hv);
+        return -1;
+    }
+    if (!P.q || !P.k || !P.v || !P.a || !P.b || !P.A_log || !P.dt_bias || !P.h0_source || !P.o) {
+        fprintf(stderr, "gdn_run_chunk_prefill: null tensor pointer\n");
+        return -1;
+    }
+    if (P.n <= 0 || P.seq_len <= 0) {
+        fprintf(stderr, "gdn_run_chunk_prefill: n and seq_len must be positive, got n=%d seq_len=%d\n", P.n,
+                P.seq_len);
+        return -1;
+    }
+    if ((P.z == nullptr) != (P.norm_w == nullptr)) {
+        fprintf(stderr, "gdn_run_chunk_prefill: pass both z and norm_w to fuse the norm, or neither\n");
+        return -1;
+    }
+    gdn::Launch L;
+    memset(&L, 0, sizeof(L));
+    L.q = P.q; L.k = P.k; L.v = P.v; L.z = P.z; L.w = P.norm_w; L.eps = P.eps; L.out = P.o;
+    L.s0 = P.h0_source; L.sf = P.h0_source;  // initial state in, final state out, in place
+    L.nseq = P.n; L.B = P.n; L.T = P.seq_len; L.HV = P.hv; L.HQK = P.h; L.DK = P.k_dim; L.DV = P.v_dim;
+    L.chunk = gdn::CS; L.max_nc = (P.seq_len + gdn::CS - 1) / gdn::CS;
+    L.ws = P.workspace; L.ws_bytes = P.workspace_bytes; L.stream = stream;
+    L.prestage = 1; L.ga = P.a; L.gb = P.b; L.A_log = P.A_log; L.dt_bias = P.dt_bias;
+    const cudaError_t e = gdn::launch(L);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "gdn_run_chunk_prefill: %s\n", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
 }
 
 cudaError_t deltanet_read_status(void* workspace, int* status_host, int clear, cudaStream_t stream) {

@@ -31,10 +31,20 @@ SIGNATURES = {
                                       + [c_void_p, c_size_t, c_void_p]),
     "deltanet_chunk_prefill_gated_noalloc": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p, c_void_p]
                                              + [c_int] * 7 + [c_void_p]),
+    "gdn_run_chunk_prefill": (c_int, [c_void_p, c_void_p]),
     "gated_rmsnorm_forward": (c_int, [c_void_p] * 4 + [c_int64, c_int, c_float, c_int, c_void_p]),
     "deltanet_read_status": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
     "gdn_b200_version": (ctypes.c_char_p, []),
 }
+
+
+class GdnPrefillParams(ctypes.Structure):
+    """Mirror of ``gdn_prefill_params`` (include/gdn_prefill.h)."""
+    _fields_ = [("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("a", c_void_p), ("b", c_void_p),
+                ("A_log", c_void_p), ("dt_bias", c_void_p), ("h0_source", c_void_p), ("o", c_void_p),
+                ("z", c_void_p), ("norm_w", c_void_p), ("eps", c_float),
+                ("n", c_int), ("seq_len", c_int), ("h", c_int), ("hv", c_int), ("k_dim", c_int), ("v_dim", c_int),
+                ("workspace", c_void_p), ("workspace_bytes", c_size_t)]
 
 
 class GdnLibraryError(RuntimeError):

@@ -19,7 +19,7 @@ import torch
 from ._lib import cuda_error_string, load_library
 
 __all__ = ["chunk_prefill", "chunk_prefill_debug", "chunk_prefill_gated", "chunk_prefill_varlen",
-           "gated_rmsnorm", "chunk_gated_delta_rule_fast", "workspace_size", "GdnError", "read_status"]
+           "run_chunk_prefill", "gated_rmsnorm", "chunk_gated_delta_rule_fast", "workspace_size", "GdnError", "read_status"]
 
 CHUNK = 64
 HEAD_DIM = 128
@@ -235,6 +235,35 @@ def gated_rmsnorm(o, z, w, eps: float = 1e-6):
                                      0 if o.dtype == torch.float16 else 1, _stream())
     _check(code, "gated_rmsnorm_forward")
     return y
+
+
+def run_chunk_prefill(q, k, v, a, b, A_log, dt_bias, h0, z=None, norm_w=None, eps: float = 1e-6):
+    """The reference's TRT prefill adapter (runGdnChunkPrefillSm87, gdnChunkPrefillSm87.cu:186-320) as one
+    fused launch: fp16 q/k [n,T,h,128] (not normalised), v [n,T,hv,128], a/b [n,T,hv], dt_bias [hv],
+    fp32 A_log [hv]; h0 fp32 [n,hv,128,128] holds the initial state and receives the final state in place.
+    Returns o (fp16 [n,T,hv,128]), or y when z and norm_w (fp16) are given."""
+    for t in (q, k, v, a, b, dt_bias) + ((z, norm_w) if z is not None else ()):
+        if t.dtype != torch.float16 or not t.is_cuda:
+            raise ValueError("q, k, v, a, b, dt_bias (and z, norm_w) must be fp16 CUDA tensors")
+    if A_log.dtype != torch.float32 or h0.dtype != torch.float32 or not h0.is_contiguous():
+        raise ValueError("A_log must be fp32 and h0 a contiguous fp32 tensor")
+    from ._lib import GdnPrefillParams
+    lib = load_library()
+    n, T, h, kd = q.shape
+    hv, vd = v.shape[2], v.shape[3]
+    q, k, v, a, b, A_log, dt_bias = (t.contiguous() for t in (q, k, v, a, b, A_log, dt_bias))
+    if z is not None:
+        z, norm_w = z.contiguous(), norm_w.contiguous()
+    o = torch.empty_like(v)
+    ws = _workspace(q.device, workspace_size(n, T, hv))
+    prm = GdnPrefillParams(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), a=a.data_ptr(), b=b.data_ptr(),
+                           A_log=A_log.data_ptr(), dt_bias=dt_bias.data_ptr(), h0_source=h0.data_ptr(),
+                           o=o.data_ptr(), z=None if z is None else z.data_ptr(),
+                           norm_w=None if norm_w is None else norm_w.data_ptr(), eps=float(eps), n=n, seq_len=T, h=h,
+                           hv=hv, k_dim=kd, v_dim=vd, workspace=ws.data_ptr(), workspace_bytes=ws.numel())
+    if lib.gdn_run_chunk_prefill(ctypes.byref(prm), _stream()) != 0:
+        raise GdnError("gdn_run_chunk_prefill failed (see stderr)")
+    return o
 
 
 def _l2norm_fp32(x):
