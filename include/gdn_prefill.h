@@ -140,6 +140,23 @@ typedef struct gdn_prefill_params {
  * success, -1 (with a message on stderr) on failure, as the reference. */
 int gdn_run_chunk_prefill(const gdn_prefill_params* params, cudaStream_t stream);
 
+/* Decode form: T tokens per sequence processed one after another against
+ * `state` ([B, HV, DK, DV] fp32, read and updated in place), with the same
+ * q/k/v/g/beta layouts as the prefill and an optional fused gated RMSNorm
+ * (z and norm_w both set: out receives y, else o). Per token:
+ *   S <- S e^{g}; kv = S^T k; delta = (v - kv) beta; S <- S + k delta^T; o = S^T q / sqrt(DK).
+ * Continues a prefill: passing its final state gives the same outputs as a
+ * longer prefill. No counterpart in the reference, which leaves decode to stock
+ * Edge-LLM (export/patches/orin_text_engine/README.md:15); the semantics are
+ * transformers' torch_recurrent_gated_delta_rule. */
+cudaError_t deltanet_recurrent_decode(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    const void* z, const void* norm_w, float eps,
+    void* out, float* state,
+    int B, int T, int HV, int HQK, int DK, int DV,
+    cudaStream_t stream);
+
 /* Standalone gated RMSNorm over rows of dv: y = w * round(o * rsqrt(mean(o^2)+eps)) * silu(z).
  * dtype 0 = fp16 I/O (the reference plugin's only format,
  * gatedRmsNormPlugin.cpp:155-167), 1 = bf16 I/O. Replaces

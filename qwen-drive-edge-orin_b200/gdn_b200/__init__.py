@@ -9,6 +9,7 @@ and ``kernels/harness/chunk_delta.py``):
 * :func:`chunk_prefill_gated` ``(q, k, v, g, beta, z, w, s0=None, eps=1e-6) -> [y, sf]``
 * :func:`chunk_prefill_varlen` ``(q, k, v, g, beta, cu_seqlens, s0=None, z=None, w=None, eps=1e-6)``
 * :func:`run_chunk_prefill` (the TRT adapter's fp16 inputs, pre-stage fused)
+* :func:`recurrent_decode` (single/few-token recurrent update, state in place)
 * :func:`gated_rmsnorm` ``(o, z, w, eps=1e-6) -> y``
 * :func:`chunk_gated_delta_rule_fast` (transformers-compatible signature)
 
@@ -21,6 +22,7 @@ from .binding import (  # noqa: F401
     chunk_prefill_gated,
     chunk_prefill_varlen,
     run_chunk_prefill,
+    recurrent_decode,
     gated_rmsnorm,
     chunk_gated_delta_rule_fast,
     workspace_size,

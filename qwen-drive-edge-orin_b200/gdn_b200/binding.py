@@ -19,7 +19,7 @@ import torch
 from ._lib import cuda_error_string, load_library
 
 __all__ = ["chunk_prefill", "chunk_prefill_debug", "chunk_prefill_gated", "chunk_prefill_varlen",
-           "run_chunk_prefill", "gated_rmsnorm", "chunk_gated_delta_rule_fast", "workspace_size", "GdnError", "read_status"]
+           "run_chunk_prefill", "recurrent_decode", "gated_rmsnorm", "chunk_gated_delta_rule_fast", "workspace_size", "GdnError", "read_status"]
 
 CHUNK = 64
 HEAD_DIM = 128
@@ -264,6 +264,26 @@ def run_chunk_prefill(q, k, v, a, b, A_log, dt_bias, h0, z=None, norm_w=None, ep
     if lib.gdn_run_chunk_prefill(ctypes.byref(prm), _stream()) != 0:
         raise GdnError("gdn_run_chunk_prefill failed (see stderr)")
     return o
+
+
+def recurrent_decode(q, k, v, g, beta, state, z=None, w=None, eps: float = 1e-6):
+    """Decode step(s): q/k bf16 [B,T,HQK,128], v bf16 [B,T,HV,128], g/beta fp32 [B,T,HV]; the fp32
+    ``state`` [B,HV,128,128] (e.g. a prefill's final state) is updated in place. Returns o (or y with
+    z, w bf16) [B,T,HV,128]; semantics of transformers ``torch_recurrent_gated_delta_rule``."""
+    B, T, HQK, HV = _check_inputs(q, k, v, g, beta)
+    if state.dtype != torch.float32 or not state.is_contiguous() or tuple(state.shape) != (B, HV, HEAD_DIM, HEAD_DIM):
+        raise ValueError("state must be a contiguous fp32 [B, HV, 128, 128] tensor")
+    if (z is None) != (w is None):
+        raise ValueError("pass both z and w (fused norm) or neither")
+    lib = load_library()
+    q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
+    if z is not None:
+        z, w = z.contiguous(), w.contiguous()
+    out = torch.empty_like(v)
+    code = lib.deltanet_recurrent_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w), float(eps),
+                                         _ptr(out), _ptr(state), B, T, HV, HQK, HEAD_DIM, HEAD_DIM, _stream())
+    _check(code, "deltanet_recurrent_decode")
+    return out
 
 
 def _l2norm_fp32(x):

@@ -306,3 +306,34 @@ def test_adapter_fused_prestage(n, T, h, hv):
     assert np.isfinite(y).all()
     assert m["norm_rel"] < 5e-3, m
     assert m["y_l2"] < 1e-2 and m["y_cos_masked"] >= COS_MIN, m
+
+
+# ------------------------------------------------------------------ decode step
+@pytest.mark.parametrize("B,T,HQK,HV,gated", [(1, 1, 1, 2, False), (2, 3, 2, 4, True), (1, 4, 16, 32, True)])
+def test_recurrent_decode(B, T, HQK, HV, gated):
+    """deltanet_recurrent_decode against transformers torch_recurrent_gated_delta_rule (oracle)."""
+    inp = make_inputs(B, T, HQK, HV, 128, seed=500 + T * B, dist="baseline", with_s0=True)
+    o_ref, sf_ref = O.recurrent_gated_delta_rule(inp.q, inp.k, inp.v, inp.g, inp.beta, inp.s0)
+    st = dev(inp.s0, torch.float32)
+    out = gdn_b200.recurrent_decode(dev(inp.q), dev(inp.k), dev(inp.v), dev(inp.g, torch.float32),
+                                    dev(inp.beta, torch.float32), st, dev(inp.z) if gated else None,
+                                    dev(inp.w) if gated else None, inp.eps)
+    torch.cuda.synchronize()
+    if gated:
+        check_y(host(out), O.gated_rmsnorm(o_ref, inp.z, inp.w, inp.eps), f"decode-y B{B} T{T}")
+        assert tensor_l2_rel(host(st), sf_ref) <= STATE_REL
+    else:
+        check_o(host(out), o_ref, host(st), sf_ref, f"decode B{B} T{T}")
+
+
+def test_prefill_then_decode_continues_the_sequence():
+    """Prefill of T tokens, then decode of 3 more from its final state, equals a prefill of T + 3."""
+    inp = make_inputs(1, 131, 2, 4, 128, seed=77, dist="refgrid", with_s0=True)
+    q, k, v = dev(inp.q), dev(inp.k), dev(inp.v)
+    g, b, s0 = dev(inp.g, torch.float32), dev(inp.beta, torch.float32), dev(inp.s0, torch.float32)
+    o_all, sf_all = gdn_b200.chunk_prefill(q, k, v, g, b, s0)
+    o_pre, sf_pre = gdn_b200.chunk_prefill(q[:, :128], k[:, :128], v[:, :128], g[:, :128], b[:, :128], s0)
+    st = sf_pre.clone()
+    o_dec = gdn_b200.recurrent_decode(q[:, 128:], k[:, 128:], v[:, 128:], g[:, 128:], b[:, 128:], st)
+    torch.cuda.synchronize()
+    check_o(host(torch.cat([o_pre, o_dec], 1)), host(o_all), host(st), host(sf_all), "prefill+decode")
