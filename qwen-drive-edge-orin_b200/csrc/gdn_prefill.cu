@@ -37,18 +37,18 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
 #include <mutex>
 
+#include "gdn_common.cuh"
 #include "gdn_prefill.h"
 #include "sm100_ptx.cuh"
 
 namespace gdn {
 
-constexpr int CS = 64;         // chunk length (tokens)
-constexpr int HD = 128;        // head dim (DK = DV)
 constexpr int NTHREADS = 256;  // 8 warps: warps w and w+4 share TMEM lane quarter w
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -71,7 +71,6 @@ constexpr uint32_t OFF_M_HI = 131072;    // M = scale (q k^T) * decay, [64][64] 
 constexpr uint32_t OFF_M_LO = 139264;
 constexpr uint32_t OFF_L = 147456;       // L / T fp32 [64][68]; o staging afterwards (8 KB/panel)
 constexpr uint32_t OFF_OST = OFF_L;
-constexpr int LSTRIDE = 68;              // 16-byte aligned rows for vector access
 constexpr uint32_t OFF_GATE = OFF_L + 64 * LSTRIDE * 4;  // 164864: w * silu(z), fp32 [64][128], 16-B chunks swizzled
 constexpr uint32_t OFF_MISC = OFF_GATE + 32768;          // 197632
 constexpr uint32_t MISC_C = 0;      // c        [64] f32
@@ -105,223 +104,10 @@ constexpr uint32_t TM_SA_LO = 448;
 // Barrier slots.
 enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4 };
 
-constexpr uint32_t WAIT_ITERS = 1u << 22;  // bounded spin (~0.3 s with backoff)
 
 // Debug record layout (floats) per (seq, head, chunk).
 constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192,
               DBG_O = DBG_VN + 8192, DBG_SC = DBG_O + 8192, DBG_REC = DBG_SC + 16384;
-
-struct Params {
-    CUtensorMap tm_q, tm_k, tm_v, tm_z;
-    const float* g;
-    const float* beta;
-    const __nv_bfloat16* w;        // norm weight [128] (gated only)
-    const float* s0;               // [NSEQ, HV, 128, 128] or null
-    float* sf;                     // [NSEQ, HV, 128, 128]
-    __nv_bfloat16* out;            // o or y, [B, T, HV, 128] / [1, T, HV, 128]
-    const int* cu_seqlens;         // varlen offsets or null
-    unsigned int* status;          // workspace status word
-    float* dbg;                    // debug records or null
-    int T;                         // tokens per batch row (fixed) / total tokens (varlen)
-    int HV, HQK;
-    int max_nc;                    // chunks of the longest sequence (debug indexing)
-    float scale;                   // 1/sqrt(DK)
-    float eps;
-    int gated;
-    // Pre-stage mode (the reference's TRT adapter inputs): q/k/v/z/w and the
-    // output are fp16, q/k arrive un-normalised (L2-normalised here in fp32 and
-    // rounded to bf16), v is rounded to bf16, and the gates are computed from
-    // a, b (fp16 [.., HV]), A_log (fp32 [HV]) and dt_bias (fp16 [HV]).
-    int prestage;
-    const __half* ga;
-    const __half* gb;
-    const float* A_log;
-    const __half* dt_bias;
-};
-
-// Byte offset of bf16 element (row, col) in a 128B-swizzled tile whose panels
-// hold `rows` rows each.
-__device__ __forceinline__ uint32_t sw_off(int row, int col, int rows) {
-    return (uint32_t)((col >> 6) * rows * 128 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) +
-                      ((col & 7) << 1));
-}
-// Byte offset of fp32 element group [4j, 4j+4) of row `row` in the [64][128] fp32 gate
-// tile: the 16-byte chunk index is XOR-swizzled with the row inside each group of 8.
-__device__ __forceinline__ uint32_t gate_chunk(int row, int j) {
-    return (uint32_t)(row * 512 + (((j & ~7) | ((j ^ row) & 7)) << 4));
-}
-// Byte offset of the 16-byte chunk holding cols [8*ch, 8*ch+8) of `row`.
-__device__ __forceinline__ uint32_t sw_chunk(int row, int ch, int rows) {
-    return (uint32_t)((ch >> 3) * rows * 128 + row * 128 + (((ch & 7) ^ (row & 7)) << 4));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
-__device__ __forceinline__ float bf16r(float x) {
-    return __bfloat162float(__float2bfloat16_rn(x));
-}
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
-                 "r"(d)
-                 : "memory");
-}
-__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c,
-                                             uint32_t& d) {
-    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
-                 : "r"(addr)
-                 : "memory");
-}
-__device__ __forceinline__ float ex2f(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float rcpf(float x) {
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-constexpr float LOG2E = 1.4426950408889634f;
-
-// Split two fp32 values into packed bf16 hi parts and packed bf16 lo parts
-// (x = hi + lo to ~16 mantissa bits).
-__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    hi = *reinterpret_cast<const uint32_t*>(&h);
-    lo = pack_bf16(a - __low2float(h), b - __high2float(h));
-}
-
-// Write 8 consecutive fp32 values as bf16 hi (and optionally lo) parts into a
-// 16-byte chunk of two tiles.
-__device__ __forceinline__ void put8_split(uint32_t hi_addr, uint32_t lo_addr, const float* x,
-                                           bool want_lo) {
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) split2(x[2 * i], x[2 * i + 1], h[i], l[i]);
-    st_shared_v4(hi_addr, h[0], h[1], h[2], h[3]);
-    if (want_lo) st_shared_v4(lo_addr, l[0], l[1], l[2], l[3]);
-}
-
-// ---------------------------------------------------------------------------
-// T = (I + L)^-1 for a 64x64 strictly-lower L held in Ls (stride 68), in place.
-//   A: the four 16x16 diagonal blocks by forward substitution (one warp each,
-//      lane = column, column in registers);
-//   B/C: 32x32 halves: T_10 = -(T_11 L_10) T_00 and T_32 = -(T_33 L_32) T_22;
-//   D/E: T_[32:,:32] = -(T_[32:,32:] L_[32:,:32]) T_[:32,:32].
-// Every product is register-blocked 1x4 with 16-byte loads and uses the
-// triangular structure to skip zero terms. X holds the left products.
-__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-__device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
-    acc.x = fmaf(a, b.x, acc.x);
-    acc.y = fmaf(a, b.y, acc.y);
-    acc.z = fmaf(a, b.z, acc.z);
-    acc.w = fmaf(a, b.w, acc.w);
-}
-
-// `idle(phase)` runs on threads 128-255 during phases A, B and C (phase = 0, 1, 2),
-// which use only threads 0-127.
-template <typename Idle>
-__device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, Idle&& idle) {
-    const int warp = tid >> 5, lane = tid & 31;
-    if (tid >= 128) idle(0);
-    // A: diagonal blocks
-    if (warp < 4 && lane < 16) {
-        const int b = warp, c = lane;
-        const float* Lb = Ls + (16 * b) * LSTRIDE + 16 * b;
-        float t[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            float a0 = (i == c) ? 1.f : 0.f, a1 = 0.f;
-#pragma unroll
-            for (int j = 0; j + 1 < i; j += 2) {
-                a0 = fmaf(-Lb[i * LSTRIDE + j], t[j], a0);
-                a1 = fmaf(-Lb[i * LSTRIDE + j + 1], t[j + 1], a1);
-            }
-            if (i & 1) a0 = fmaf(-Lb[i * LSTRIDE + i - 1], t[i - 1], a0);
-            t[i] = a0 + a1;
-        }
-        __syncwarp(0x0000ffffu);
-        float* Tb = Ls + (16 * b) * LSTRIDE + 16 * b;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) Tb[i * LSTRIDE + c] = t[i];
-    }
-    __syncthreads();
-    // B: X[0:256] = T_11 L_10, X[256:512] = T_33 L_32   (16x16 each, stride 16).
-    // Terms above the diagonal of T_rr are stored zeros, so every unit runs the
-    // full 16-term range in groups of four with its loads issued together.
-    if (tid >= 128) idle(1);
-    if (tid < 128) {
-        const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
-        const int r0 = 16 + 32 * blk, c0 = 32 * blk;  // T_rr at (r0, r0), L block at (r0, c0)
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* trow = Ls + (r0 + i) * LSTRIDE + r0;
-#pragma unroll
-        for (int m0 = 0; m0 < 16; m0 += 4) {
-            const float4 t4 = ld4(trow + m0);
-            const float4 b0 = ld4(Ls + (r0 + m0) * LSTRIDE + c0 + j0), b1 = ld4(Ls + (r0 + m0 + 1) * LSTRIDE + c0 + j0);
-            const float4 b2 = ld4(Ls + (r0 + m0 + 2) * LSTRIDE + c0 + j0), b3 = ld4(Ls + (r0 + m0 + 3) * LSTRIDE + c0 + j0);
-            fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
-        }
-        *reinterpret_cast<float4*>(X + blk * 256 + i * 16 + j0) =
-            make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
-    }
-    __syncthreads();
-    // C: T_10 = -X0 T_00 -> rows 16-31, cols 0-15; T_32 = -X1 T_22 -> rows 48-63, cols 32-47
-    if (tid >= 128) idle(2);
-    if (tid < 128) {
-        const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
-        const int d0 = 32 * blk;  // T_ss at (d0, d0)
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* xrow = X + blk * 256 + i * 16;
-#pragma unroll
-        for (int m0 = 0; m0 < 16; m0 += 4) {
-            const float4 x4 = ld4(xrow + m0);
-            const float4 b0 = ld4(Ls + (d0 + m0) * LSTRIDE + d0 + j0), b1 = ld4(Ls + (d0 + m0 + 1) * LSTRIDE + d0 + j0);
-            const float4 b2 = ld4(Ls + (d0 + m0 + 2) * LSTRIDE + d0 + j0), b3 = ld4(Ls + (d0 + m0 + 3) * LSTRIDE + d0 + j0);
-            fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
-        }
-        *reinterpret_cast<float4*>(Ls + (d0 + 16 + i) * LSTRIDE + d0 + j0) =
-            make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
-    }
-    __syncthreads();
-    // D: X[512:1536] = T_[32:,32:] L_[32:,:32]   (32x32, stride 32)
-    {
-        const int i = tid >> 3, j0 = (tid & 7) * 4;
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* trow = Ls + (32 + i) * LSTRIDE + 32;
-        const int mend = (i + 4) & ~3;  // T_[32:,32:][i][m] = 0 for m > i
-#pragma unroll 2
-        for (int m0 = 0; m0 < mend; m0 += 4) {
-            const float4 t4 = ld4(trow + m0);
-            const float4 b0 = ld4(Ls + (32 + m0) * LSTRIDE + j0), b1 = ld4(Ls + (33 + m0) * LSTRIDE + j0);
-            const float4 b2 = ld4(Ls + (34 + m0) * LSTRIDE + j0), b3 = ld4(Ls + (35 + m0) * LSTRIDE + j0);
-            fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
-        }
-        *reinterpret_cast<float4*>(X + 512 + i * 32 + j0) =
-            make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
-    }
-    __syncthreads();
-    // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j)
-    {
-        const int i = tid >> 3, j0 = (tid & 7) * 4;
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* xrow = X + 512 + i * 32;
-#pragma unroll 2
-        for (int m0 = j0; m0 < 32; m0 += 4) {
-            const float4 x4 = ld4(xrow + m0);
-            const float4 b0 = ld4(Ls + m0 * LSTRIDE + j0), b1 = ld4(Ls + (m0 + 1) * LSTRIDE + j0);
-            const float4 b2 = ld4(Ls + (m0 + 2) * LSTRIDE + j0), b3 = ld4(Ls + (m0 + 3) * LSTRIDE + j0);
-            fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
-        }
-        *reinterpret_cast<float4*>(Ls + (32 + i) * LSTRIDE + j0) =
-            make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
-    }
-    __syncthreads();
-}
 
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1017,6 +803,23 @@ static cudaError_t ensure_smem_attr() {
 
 constexpr size_t WS_HEADER = 256;
 
+cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream);  // gdn_prefill_split.cu
+int split_cluster_ctas();
+
+// Kernel choice: the cluster-split kernel when every (sequence, head) cluster
+// fits on the GPU at once (small batches are latency-bound on the state
+// chain), else the one-CTA-per-head kernel. GDN_B200_KERNEL=fused|split|auto
+// overrides (debug dumps and the pre-stage mode use the one-CTA kernel).
+static bool use_split(int nseq, int HV) {
+    const char* env = getenv("GDN_B200_KERNEL");
+    if (env && strcmp(env, "fused") == 0) return false;
+    if (env && strcmp(env, "split") == 0) return true;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
+    return (long long)nseq * HV * split_cluster_ctas() <= sms;
+}
+
 struct Launch {
     const void *q, *k, *v;
     const float *g, *beta;
@@ -1087,6 +890,7 @@ static cudaError_t launch(const Launch& L) {
     p.A_log = L.A_log;
     p.dt_bias = static_cast<const __half*>(L.dt_bias);
 
+    if (!L.dbg && !L.prestage && use_split(L.nseq, L.HV)) return launch_split(p, L.nseq, L.HV, L.stream);
     cudaError_t e = ensure_smem_attr();
     if (e != cudaSuccess) return e;
     dim3 grid(1, L.HV, L.nseq);

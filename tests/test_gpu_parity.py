@@ -337,3 +337,26 @@ def test_prefill_then_decode_continues_the_sequence():
     o_dec = gdn_b200.recurrent_decode(q[:, 128:], k[:, 128:], v[:, 128:], g[:, 128:], b[:, 128:], st)
     torch.cuda.synchronize()
     check_o(host(torch.cat([o_pre, o_dec], 1)), host(o_all), host(st), host(sf_all), "prefill+decode")
+
+
+# ------------------------------------------------------------------ both prefill kernels
+@pytest.mark.parametrize("B,T,HQK,HV,s0", [(1, 1, 1, 2, True), (1, 130, 1, 2, True), (2, 200, 2, 4, False),
+                                           (1, 1141, 16, 32, True), (3, 300, 4, 8, True)])
+def test_split_and_fused_kernels_agree(B, T, HQK, HV, s0, monkeypatch):
+    """The cluster-split kernel (prep CTAs feeding a chain CTA) and the one-CTA kernel compute the same
+    prefill: each against the oracle, and against each other."""
+    inp = make_inputs(B, T, HQK, HV, 128, seed=3000 + T + B, dist="baseline", with_s0=s0)
+    o_ref, sf_ref = O.chunk_gated_delta_rule(inp.q, inp.k, inp.v, inp.g, inp.beta, 64, inp.s0)
+    y_ref = O.gated_rmsnorm(o_ref, inp.z, inp.w, inp.eps)
+    res = {}
+    for kern in ("fused", "split"):
+        monkeypatch.setenv("GDN_B200_KERNEL", kern)
+        o, sf = run_gpu(inp)
+        y, sf2 = run_gpu(inp, gated=True)
+        check_o(o, o_ref, sf, sf_ref, f"{kern} B{B} T{T}")
+        check_y(y, y_ref, f"{kern}-y B{B} T{T}")
+        assert np.array_equal(sf, sf2)
+        res[kern] = (o, sf, y)
+    assert np.array_equal(res["fused"][0], res["split"][0]) and np.array_equal(res["fused"][1], res["split"][1])
+    assert max_rel(res["fused"][2], res["split"][2]) < Y_MAX_REL
+    assert gdn_b200.binding.read_status() == 0
