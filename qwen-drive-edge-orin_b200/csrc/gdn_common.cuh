@@ -92,6 +92,18 @@ __device__ __forceinline__ float rcpf(float x) {
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+// Read-only global loads issued where they are written: a prefetch for a later chunk must
+// not be moved by the compiler down to its first use, where its latency would be exposed.
+__device__ __forceinline__ float ldg_early(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ __half ldg_early(const __half* p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.b16 %0, [%1];" : "=h"(v) : "l"(p));
+    return __ushort_as_half(v);
+}
 constexpr float LOG2E = 1.4426950408889634f;
 
 // Split two fp32 values into packed bf16 hi parts and packed bf16 lo parts
@@ -130,9 +142,11 @@ __device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
 }
 
 // `idle(phase)` runs on threads 128-255 during phases A, B and C (phase = 0, 1, 2),
-// which use only threads 0-127.
-template <typename Idle>
-__device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, Idle&& idle) {
+// which use only threads 0-127. `sync()` is the barrier over the 256 threads taking
+// part (a block-wide __syncthreads, or a named barrier when other warps of the
+// block do different work).
+template <typename Idle, typename Sync>
+__device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, Idle&& idle, Sync&& sync) {
     const int warp = tid >> 5, lane = tid & 31;
     if (tid >= 128) idle(0);
     // A: diagonal blocks
@@ -156,7 +170,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
 #pragma unroll
         for (int i = 0; i < 16; ++i) Tb[i * LSTRIDE + c] = t[i];
     }
-    __syncthreads();
+    sync();
     // B: X[0:256] = T_11 L_10, X[256:512] = T_33 L_32   (16x16 each, stride 16).
     // Terms above the diagonal of T_rr are stored zeros, so every unit runs the
     // full 16-term range in groups of four with its loads issued together.
@@ -176,7 +190,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
         *reinterpret_cast<float4*>(X + blk * 256 + i * 16 + j0) =
             make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
     }
-    __syncthreads();
+    sync();
     // C: T_10 = -X0 T_00 -> rows 16-31, cols 0-15; T_32 = -X1 T_22 -> rows 48-63, cols 32-47
     if (tid >= 128) idle(2);
     if (tid < 128) {
@@ -194,7 +208,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
         *reinterpret_cast<float4*>(Ls + (d0 + 16 + i) * LSTRIDE + d0 + j0) =
             make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
     }
-    __syncthreads();
+    sync();
     // D: X[512:1536] = T_[32:,32:] L_[32:,:32]   (32x32, stride 32)
     {
         const int i = tid >> 3, j0 = (tid & 7) * 4;
@@ -211,7 +225,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
         *reinterpret_cast<float4*>(X + 512 + i * 32 + j0) =
             make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
     }
-    __syncthreads();
+    sync();
     // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j)
     {
         const int i = tid >> 3, j0 = (tid & 7) * 4;
@@ -227,7 +241,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
         *reinterpret_cast<float4*>(Ls + (32 + i) * LSTRIDE + j0) =
             make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
     }
-    __syncthreads();
+    sync();
 }
 
 }  // namespace gdn

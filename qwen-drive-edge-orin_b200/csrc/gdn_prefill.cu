@@ -252,28 +252,44 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         load_v(0);
     }
     if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)
-    // Gates of the next chunk are prefetched into warp 0's registers (lane l: tokens 2l, 2l+1).
-    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
+    // Gate inputs of the next chunk are prefetched into warp 0's registers (lane l: tokens 2l,
+    // 2l+1) as raw values: loaded unconditionally (positions past the sequence end are clamped
+    // to its last token), transformed and masked only when that chunk is processed, so that
+    // nothing waits on these loads earlier.
+    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;         // g, beta
+    __half an0 = __float2half(0.f), an1 = an0, bh0 = an0, bh1 = an0;  // pre-stage a, b
     // Pre-stage gate math (gdnChunkPrefillSm87.cu:44-49, 113-125):
     // g = -exp(A_log[h]) * softplus(a + dt_bias[h]) (threshold 20), beta = sigmoid(b).
     const float gA = p.prestage ? -expf(__ldg(p.A_log + h)) : 0.f;
     const float gdt = p.prestage ? __half2float(p.dt_bias[h]) : 0.f;
-    auto gate_of = [&](size_t i, float& gv, float& bv) {
+    auto load_gates = [&](int n) {
+        const int last = len - n * CS - 1;
+        const long long t0 = tok_base + (long long)n * CS;
+        const size_t i0 = (size_t)(t0 + min(2 * lane, last)) * p.HV + h;
+        const size_t i1 = (size_t)(t0 + min(2 * lane + 1, last)) * p.HV + h;
         if (p.prestage) {
-            const float x = __half2float(p.ga[i]) + gdt;
-            gv = gA * (x > 20.f ? x : log1pf(expf(x)));
-            bv = 1.f / (1.f + expf(-__half2float(p.gb[i])));
+            an0 = ldg_early(p.ga + i0);
+            bh0 = ldg_early(p.gb + i0);
+            an1 = ldg_early(p.ga + i1);
+            bh1 = ldg_early(p.gb + i1);
         } else {
-            gv = __ldg(p.g + i);
-            bv = __ldg(p.beta + i);
+            gn0 = ldg_early(p.g + i0);
+            bn0 = ldg_early(p.beta + i0);
+            gn1 = ldg_early(p.g + i1);
+            bn1 = ldg_early(p.beta + i1);
         }
     };
-    auto load_gates = [&](int n) {
-        const int valid = min(CS, len - n * CS);
-        const long long t0 = tok_base + (long long)n * CS;
-        gn0 = gn1 = bn0 = bn1 = 0.f;
-        if (2 * lane < valid) gate_of((size_t)(t0 + 2 * lane) * p.HV + h, gn0, bn0);
-        if (2 * lane + 1 < valid) gate_of((size_t)(t0 + 2 * lane + 1) * p.HV + h, gn1, bn1);
+    auto gate_of = [&](bool valid, float g_raw, float b_raw, __half a_raw, __half bb_raw, float& gv, float& bv) {
+        if (!valid) {
+            gv = bv = 0.f;
+        } else if (p.prestage) {
+            const float x = __half2float(a_raw) + gdt;
+            gv = gA * (x > 20.f ? x : log1pf(expf(x)));
+            bv = 1.f / (1.f + expf(-__half2float(bb_raw)));
+        } else {
+            gv = g_raw;
+            bv = b_raw;
+        }
     };
     if (warp == 0 && NC > 0) load_gates(0);
     ptx::tmem_wait_st();
@@ -297,7 +313,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 
         // ---- gates: in-chunk inclusive cumsum of g (warp scan), decay factors ----
         if (warp == 0) {
-            const float g0 = gn0, g1 = gn1, b0 = bn0, b1 = bn1;
+            float g0, g1, b0, b1;
+            gate_of(2 * lane < valid, gn0, bn0, an0, bh0, g0, b0);
+            gate_of(2 * lane + 1 < valid, gn1, bn1, an1, bh1, g1, b1);
             if (n + 1 < NC) load_gates(n + 1);  // overlaps the rest of this chunk
             float s = g0 + g1;
 #pragma unroll
@@ -438,7 +456,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
             }
         };
-        invert_unit_lower(Ls, X, tid, gate_work);
+        invert_unit_lower(Ls, X, tid, gate_work, [] { __syncthreads(); });
         if (rec) {
             for (int e = tid; e < CS * CS; e += NTHREADS) rec[DBG_T + e] = Ls[(e >> 6) * LSTRIDE + (e & 63)];
             if (tid < CS) rec[DBG_C + tid] = c_s[tid];
@@ -805,11 +823,14 @@ constexpr size_t WS_HEADER = 256;
 
 cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream);  // gdn_prefill_split.cu
 int split_cluster_ctas();
+bool split_available();
 
 // Kernel choice: the cluster-split kernel when every (sequence, head) cluster
 // fits on the GPU at once (small batches are latency-bound on the state
 // chain), else the one-CTA-per-head kernel. GDN_B200_KERNEL=fused|split|auto
-// overrides (debug dumps and the pre-stage mode use the one-CTA kernel).
+// overrides (debug dumps and the pre-stage mode use the one-CTA kernel). A forced
+// split launch fails with cudaErrorNotSupported when the compiled split kernel does
+// not have the register count its register split is written for.
 static bool use_split(int nseq, int HV) {
     const char* env = getenv("GDN_B200_KERNEL");
     if (env && strcmp(env, "fused") == 0) return false;
@@ -817,7 +838,7 @@ static bool use_split(int nseq, int HV) {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
-    return (long long)nseq * HV * split_cluster_ctas() <= sms;
+    return (long long)nseq * HV * split_cluster_ctas() <= sms && split_available();
 }
 
 struct Launch {

@@ -1,18 +1,35 @@
 // Cluster-split variant of the chunked gated-delta-rule prefill for small
 // batches (few (sequence, v-head) units relative to the 148 SMs).
 //
-// Each (sequence, v-head) runs on a cluster of 1 + NP CTAs:
+// Each (sequence, v-head) runs on a cluster of NP + 2 CTAs:
 //   * rank 0, the chain CTA, owns the recurrent state and runs only the
 //     state-dependent steps of every chunk: C12 (v_new), C3/C4 (output and
-//     state increment), the state update and the gated-RMSNorm epilogue;
+//     state increment) and the state update, and stages o as bf16;
 //   * ranks 1..NP, the prep CTAs, run the state-independent chunk math for
 //     chunks n = rank-1, rank-1+NP, ...: gates, P1 ([Q;K]K^T), L and M, the
-//     triangular inverse, T' and T'', P3 (W), and ship T' / W / M / decay
-//     factors into the chain CTA's slot buffer with one shared-to-shared bulk
-//     copy per chunk (completing on the chain's mbarrier; no multicast).
-// Prep and chain of different chunks overlap, so the chain's period per
-// chunk is its own work only. The math, precision scheme and operand
-// layouts are those of gdn_prefill_kernel (gdn_prefill.cu).
+//     triangular inverse, T' and T'', P3 (W), and ship them into the chain
+//     CTA's slot buffers with shared-to-shared bulk copies (completing on the
+//     chain's mbarriers; no multicast). A slot has two parts that are handed
+//     back separately: part A (T', W, decay factors) once C12 has read it,
+//     part B (M) once the intra-chunk output term has;
+//   * rank NP+1, the output CTA, receives each chunk's staged o the same way
+//     and runs the gated-RMSNorm epilogue (z tiles, norm weight, y stores).
+// Prep, chain and output work of different chunks overlap, so the chain's
+// period per chunk is its own work only.
+//
+// Inside the chain CTA the work is split by warp. A tcgen05.mma issue does
+// not return before the tensor core has (nearly) executed the instruction,
+// so the issuing warp is busy for the whole MMA time; warp 8 does only that,
+// warp 9 issues the TMA loads and hands slot parts back as soon as their
+// buffers are free, and warps 0-7 read and write TMEM and run the CUDA-core
+// steps. Per chunk n the issue order is C12(n) (its state-independent half
+// first), S^T q^T(n), then - once warps 0-7 have formed the v_new operands -
+// dS(n) and v_new^T M^T(n); warps 0-7 form v_new(n), update the state, then
+// read the output back and stage it, which overlaps C12 and S^T q^T of chunk
+// n+1. The hand-offs between the groups are mbarriers with bounded waits.
+//
+// The math, precision scheme and operand layouts are those of
+// gdn_prefill_kernel (gdn_prefill.cu).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -26,41 +43,80 @@
 namespace gdn {
 namespace split {
 
-constexpr int NTHREADS = 256;
-constexpr int NP = 2;  // prep CTAs per cluster
+constexpr int NCOMPUTE = 256;             // warpgroups 0-1: TMEM and CUDA-core work
+constexpr int NTHREADS = NCOMPUTE + 128;  // warpgroup 2 (chain CTA): warp 8 MMA issue, warp 9 TMA / slots
+constexpr int ISSUER_WARP = NCOMPUTE / 32;
+// Registers: 168 per thread at launch (384 threads fill the 64K file); warpgroup 2 gives
+// part of its share to warpgroups 0-1: 2 x 128 x 192 + 128 x 120 = 384 x 168. The MMA
+// warp keeps the unrolled MMA descriptors in registers, hence its 120.
+constexpr int LAUNCH_REGS = 168, COMPUTE_REGS = 192, ISSUE_REGS = 120;
+static_assert(2 * 128 * COMPUTE_REGS + 128 * ISSUE_REGS <= NTHREADS * LAUNCH_REGS, "register split exceeds the pool");
+constexpr uint32_t CSYNC = 1;            // named barrier of warps 0-7
+constexpr int NP = 2;                    // prep CTAs per cluster
+constexpr uint32_t OUT_RANK = NP + 1;    // the output CTA
+constexpr int CLUSTER = NP + 2;          // chain, NP prep CTAs, output
 
-// ---- slot layout (identical in the prep CTA's staging and the chain CTA's slots)
+// ---- prep CTA staging layout (one chunk's shipment)
 constexpr uint32_t SL_TP = 0;        // [T'_hi; T'_lo] 128 rows x 64 cols bf16 (K-major, stacked along N)
 constexpr uint32_t SL_W = 16384;     // W^T hi, lo: [128 dk][64 tok] bf16 MN-major tiles, 16 KB apart
 constexpr uint32_t SL_M = 49152;     // M hi, lo: [64][64] bf16, 8 KB apart
 constexpr uint32_t SL_EC = 65536;    // e^c      [64] f32
 constexpr uint32_t SL_ED = 65792;    // e^{cL-c} [64] f32
-constexpr uint32_t SL_BYTES = 66048; // bytes shipped per chunk
-constexpr uint32_t SLOT = 66560;     // slot stride (1024-aligned)
+constexpr uint32_t SLOT = 66560;     // staging stride (1024-aligned)
+// ---- chain CTA slot layout: part A = staging [SL_TP, SL_M) + [SL_EC, SL_EC + 512), part B = M
+constexpr uint32_t A_TP = 0, A_W = 16384, A_EC = 49152, A_ED = 49408;
+constexpr uint32_t A_BYTES = 49664;
+constexpr uint32_t ASLOT = 50176;    // 1024-aligned stride
+constexpr uint32_t B_BYTES = 16384;
+constexpr int NSLOT = 2;             // slot s is filled by prep CTA 1 + s
+static_assert(NSLOT == NP, "each prep CTA owns one chain slot");
+
+constexpr uint32_t O_BYTES = 16384;  // o of one chunk: [64 tok][128 dv] bf16, two 64-row panels of 8 KB
 
 // ---- chain CTA shared memory
 constexpr uint32_t C_QK = 0;          // q rows 0-63 | k rows 64-127 (16 KB/panel)
 constexpr uint32_t C_V = 32768;
-constexpr uint32_t C_Z = 49152;
-constexpr uint32_t C_SLOT = 65536;    // NP slots
-constexpr uint32_t C_OST = C_SLOT + NP * SLOT;   // o staging [64 tok][128 dv] bf16 (8 KB/panel)
-constexpr uint32_t C_MISC = C_OST + 16384;
+constexpr uint32_t C_OST = 49152;     // 2 o staging buffers (chunk parity), shipped to the output CTA
+constexpr uint32_t C_ASLOT = C_OST + 2 * O_BYTES;       // NSLOT part-A slots
+constexpr uint32_t C_BSLOT = C_ASLOT + NSLOT * ASLOT;   // NSLOT part-B slots (M)
+constexpr uint32_t C_MISC = C_BSLOT + NSLOT * B_BYTES;
 // ---- prep CTA shared memory
 constexpr uint32_t P_QK = 0;
 constexpr uint32_t P_L = 32768;                  // L / T fp32 [64][68]
 constexpr uint32_t P_TPP = 50176;                // T'' hi, lo [64][64] bf16
 constexpr uint32_t P_STG = 66560;                // 2 staging slots
 constexpr uint32_t P_MISC = P_STG + 2 * SLOT;
-// ---- misc (both roles)
-constexpr uint32_t M_C = 0, M_BETA = 256, M_W = 512, M_BAR = 1024, M_TMEM = 1152, M_FLAG = 1156, M_BYTES = 1280;
-constexpr uint32_t SMEM_BYTES = (C_MISC > P_MISC ? C_MISC : P_MISC) + M_BYTES;
+// ---- output CTA shared memory
+constexpr uint32_t U_OSLOT = 0;                  // 2 o^T slots (chunk parity), filled by the chain CTA
+constexpr uint32_t U_Z = 2 * O_BYTES;            // 2 z tiles (chunk parity)
+constexpr uint32_t U_OT = U_Z + 2 * O_BYTES;     // o [64 tok][128 dv] (two 64-row panels), transposed here
+constexpr uint32_t U_MISC = U_OT + O_BYTES;
+// ---- misc (all roles; the chain keeps e^c of two chunks in the M_C / M_BETA areas)
+constexpr uint32_t M_C = 0, M_BETA = 256, M_W = 512, M_BAR = 1024, M_TMEM = 1280, M_FLAG = 1284, M_DONE = 1288,
+                   M_BYTES = 1408;
+constexpr uint32_t MAX2(uint32_t a, uint32_t b) { return a > b ? a : b; }
+constexpr uint32_t SMEM_BYTES = MAX2(MAX2(C_MISC, P_MISC), U_MISC) + M_BYTES;
 constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory limit");
 static_assert(P_L + 64 * LSTRIDE * 4 <= P_TPP, "L scratch overlaps T''");
 
-// barrier slots
-enum { B_Q = 0, B_K = 1, B_V = 2, B_Z = 3, B_MMA = 4, B_FULL = 5 /* chain: NP slots */, B_EMPTY = 5 /* prep */ };
-constexpr int NBAR = B_FULL + NP;
+// barrier slots: TMA tiles; MMA commit groups (chain: B_VT = v^T T'^T, the part of C12 that
+// reads the v tile, B_MMA = C12, X1 = S^T q^T + dS, Y = v_new^T M^T; B_DRAIN only on the
+// abort path); chain hand-offs from warps 0-7 to the
+// MMA / producer warps (one arrival per thread): v_new operands formed, new state operand stored,
+// output accumulators read. Per role, the barriers from B_FULLA up: chain - slot parts filled
+// by the prep CTAs, o staging buffers handed back by the output CTA; prep - slot parts handed
+// back; output - o slots filled by the chain CTA, z tiles loaded.
+enum {
+    B_Q = 0, B_K = 1, B_V = 2, B_MMA = 3, B_X1 = 4, B_Y = 5, B_DRAIN = 6,
+    B_VNR = 7, B_SOP = 8, B_OFREE = 9, B_VT = 10,
+    B_FULLA = 11 /* chain: NSLOT */, B_FULLB = B_FULLA + NSLOT /* chain: NSLOT */,
+    B_EMPTYO = B_FULLB + NSLOT /* chain: 2 */,
+    B_EMPTYA = 11 /* prep */, B_EMPTYB = 12 /* prep */,
+    B_FULLO = 11 /* output: 2 */, B_ZT = 13 /* output: 2 */
+};
+constexpr int NBAR = B_EMPTYO + 2;
+static_assert(M_BAR + 8 * NBAR <= M_TMEM, "barriers overlap the TMEM address word");
 
 // ---- TMEM
 // chain: [0,128) C12 [hi | lo] -> v_new^T hi/lo [0,64) + (v_new e^{cL-c})^T hi/lo [64,128);
@@ -76,10 +132,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                                                ~uintptr_t(1023));
     const uint32_t sb = ptx::smem_u32(smem);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quarter = warp & 3, half = warp >> 2;
+    const bool compute = (warp < ISSUER_WARP);
+    const int quarter = warp & 3, half = (warp >> 2) & 1;  // TMEM lane quarter / column half (warps 0-7)
     const int row = quarter * 32 + lane;
     const uint32_t rank = ptx::cluster_ctarank();
     const bool chain = (rank == 0);
+    const bool outcta = (rank == OUT_RANK);
     const int h = blockIdx.y;
     const int seq = blockIdx.z;
     const int hq = h / (p.HV / p.HQK);
@@ -97,22 +155,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     const int NC = (len + CS - 1) / CS;
     const long long tok_base = (long long)bcoord * p.T + t_begin;
 
-    const uint32_t misc_off = chain ? C_MISC : P_MISC;
+    const uint32_t misc_off = chain ? C_MISC : (outcta ? U_MISC : P_MISC);
     float* misc = reinterpret_cast<float*>(smem + misc_off);
     float* c_s = misc + M_C / 4;
     float* beta_s = misc + M_BETA / 4;
     float* w_s = misc + M_W / 4;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + misc_off + M_FLAG);
+    volatile int* done_flag = reinterpret_cast<volatile int*>(smem + misc_off + M_DONE);
     const uint32_t bar0 = sb + misc_off + M_BAR;
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
-    const uint32_t tmem_cols = chain ? 512u : 256u;
+    const uint32_t tmem_cols = chain ? 512u : (outcta ? 0u : 256u);
 
     if (tid == 0) {
-        for (int i = 0; i < NBAR; ++i) ptx::mbar_init(bar(i), 1);
+        for (int i = 0; i < NBAR; ++i)
+            ptx::mbar_init(bar(i), (chain && i >= B_VNR && i <= B_OFREE) ? (uint32_t)NCOMPUTE : 1u);
         ptx::fence_mbar_init();
         *abort_flag = 0;
+        *done_flag = 0;
     }
-    if (warp == 0) {
+    if (warp == 0 && tmem_cols > 0) {
         ptx::tmem_alloc(sb + misc_off + M_TMEM, tmem_cols);
         ptx::tmem_relinquish();
     }
@@ -135,9 +196,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         wait_bar(B_MMA, consumed[B_MMA] & 1u);
         ptx::tc_fence_after();
     };
-    auto commit = [&]() {
-        ptx::mma_commit(bar(B_MMA));
-        ++issued[B_MMA];
+    auto commit_to = [&](int b) {
+        ptx::mma_commit(bar(b));
+        ++issued[b];
+    };
+    auto commit = [&]() { commit_to(B_MMA); };
+    auto csync = [] { ptx::named_sync(CSYNC, NCOMPUTE); };
+    // exit decision of warps 0-7: the OR of every thread's view of the flag, taken at a barrier
+    auto vote_abort = [&] { return ptx::named_sync_or(CSYNC, NCOMPUTE, *abort_flag != 0); };
+    // warps 0-7 -> warpgroup 2 hand-off, after this thread's TMEM accesses have completed
+    auto hand_off = [&](int b) {
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(b));
     };
     auto load_tile = [&](int b, uint32_t dst, const CUtensorMap* map, int head, int n) {
         ++issued[b];
@@ -150,6 +220,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     // q -> rows 0-63 and k -> rows 64-127 of the 128-row qk panels; v, z -> 64-row panels
     auto load_q = [&](int n) { load_tile(B_Q, C_QK, &p.tm_q, hq, n); };
     auto load_k = [&](int n) { load_tile(B_K, C_QK + 8192, &p.tm_k, hq, n); };
+    auto load_v = [&](int n) { load_tile(B_V, C_V, &p.tm_v, h, n); };
+    // L2 prefetch of a later chunk's tile (both 64-column boxes), so that its TMA load is an L2 hit
+    auto prefetch_tile = [&](const CUtensorMap* map, int head, int n) {
+        if (n * CS >= len) return;
+        const int t = t_begin + n * CS;
+        ptx::tma_prefetch_4d(map, 0, head, t, bcoord);
+        ptx::tma_prefetch_4d(map, 64, head, t, bcoord);
+    };
 
     constexpr uint32_t ID_P = ptx::idesc_bf16(128, 64, 0, 0, 0);
     constexpr uint32_t ID_W = ptx::idesc_bf16(128, 128, 1, 0, 0);
@@ -158,9 +236,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);
     constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);
 
-    if (chain) {
-        // ============================== chain CTA ==============================
-        float S[64];
+    auto aslot = [](int m) { return C_ASLOT + (uint32_t)(m % NSLOT) * ASLOT; };
+    auto bslot = [](int m) { return C_BSLOT + (uint32_t)(m % NSLOT) * B_BYTES; };
+    auto slot_par = [](int m) { return (uint32_t)((m / NSLOT) & 1); };
+    if (compute) {
+        // ============================== warpgroups 0-1 ==============================
+        ptx::setmaxnreg_inc<COMPUTE_REGS>();
+        float S[64];  // chain: S[dk = 64 half + j][dv = row]
         auto store_state_operand = [&]() {
 #pragma unroll
             for (int c2 = 0; c2 < 2; ++c2) {
@@ -171,7 +253,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 ptx::tmem_st16(tl + T_SA_LO + 32 * half + 16 * c2, lo);
             }
         };
-        {
+        if (chain) {  // initial state operand
             const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
 #pragma unroll
             for (int j = 0; j < 64; ++j) {
@@ -179,175 +261,356 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 S[j] = (p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f;
             }
             store_state_operand();
+            ptx::tmem_wait_st();
+            hand_off(B_SOP);
+        } else if (outcta) {  // norm weight; arm the o slots for the first two chunks
+            if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;
+            if (tid == 0)
+                for (int s = 0; s < 2 && s < NC; ++s) {
+                    ++issued[B_FULLO + s];
+                    ptx::mbar_arrive_expect_tx(bar(B_FULLO + s), O_BYTES);
+                }
         }
-        if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;
-        const int et = tid >> 2, eq = tid & 3;
-        auto load_v = [&](int n) { load_tile(B_V, C_V, &p.tm_v, h, n); };
-        auto load_z = [&](int n) { load_tile(B_Z, C_Z, &p.tm_z, h, n); };
-        if (tid == 0) {
-            for (int s = 0; s < NP; ++s) {  // arm the slots for the first chunk of each prep CTA
-                ++issued[B_FULL + s];
-                ptx::mbar_arrive_expect_tx(bar(B_FULL + s), SL_BYTES);
-            }
-        }
-        ptx::tmem_wait_st();
         ptx::tc_fence_before();
         ptx::cluster_sync();  // every CTA's barriers are initialised and the slots armed
         ptx::tc_fence_after();
-        if (tid == 0 && NC > 0) {
-            load_q(0);
-            load_k(0);
-            load_v(0);
-            if (p.gated) load_z(0);
-        }
 
-        for (int n = 0; n < NC; ++n) {
-            if (*abort_flag) break;
-            const int valid = min(CS, len - n * CS);
-            const long long tok0 = tok_base + (long long)n * CS;
-            const uint32_t ph = (uint32_t)(n & 1);
-            const int slot = n % NP;
-            const uint32_t sp = C_SLOT + slot * SLOT;
-            const float* ec_s = reinterpret_cast<const float*>(smem + sp + SL_EC);
-            const float* ed_s = reinterpret_cast<const float*>(smem + sp + SL_ED);
+        if (chain) {
+            // ---------------- chain CTA: state, operands, output
+            float* ecl = misc + M_C / 4;  // e^c of chunks with even / odd index (M_C, M_BETA areas)
+            for (int n = 0; n < NC; ++n) {
+                if (vote_abort()) break;
+                const uint32_t ph = (uint32_t)(n & 1);
+                const float* ecn = ecl + (n & 1) * CS;
 
-            // ---- C12: v_new^T = v^T [T'_hi;T'_lo]^T - S^T [W_hi|W_lo] (hi terms cols 0-63, lo 64-127)
-            if (!ptx::mbar_wait_cluster(bar(B_FULL + slot), (uint32_t)((n / NP) & 1), WAIT_ITERS)) fail();
-            else ++consumed[B_FULL + slot];
-            wait_bar(B_V, ph);
-            if (tid == 0) {
-                ptx::tc_fence_after();
+                // ---- v_new hi/lo and (v_new e^{cL-c}) hi/lo -> TMEM A operands; keep e^c
+                wait_mma();
+                if (!ptx::mbar_wait(bar(B_FULLA + n % NSLOT), slot_par(n), WAIT_ITERS)) fail();  // decay factors landed
+                {
+                    const uint32_t sp = aslot(n);
+                    const float* ed_s = reinterpret_cast<const float*>(smem + sp + A_ED);
+                    float v[32];
+                    {
+                        float v2[32];
+                        ptx::tmem_ld32(tl + T_V + 32 * half, v);
+                        ptx::tmem_ld32(tl + T_V + 64 + 32 * half, v2);
+                        ptx::tmem_wait_ld();
 #pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint64_t a = ptx::sw128_desc(sb + C_V + s * 2048, 8192, 1024);
-                    const uint64_t b = ptx::sw128_desc(sb + sp + SL_TP + s * 32, 16, 1024);
-                    ptx::mma_bf16(tmem + T_V, a, b, ID_U, s > 0);
+                        for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
+                    }
+                    uint32_t vh[16], vl[16], ph_[16], pl[16];
+#pragma unroll
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 e4 = ld4(ed_s + 32 * half + 4 * j4);
+                        const int j = 2 * j4;
+                        split2(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
+                        split2(v[2 * j + 2], v[2 * j + 3], vh[j + 1], vl[j + 1]);
+                        split2(v[2 * j] * e4.x, v[2 * j + 1] * e4.y, ph_[j], pl[j]);
+                        split2(v[2 * j + 2] * e4.z, v[2 * j + 3] * e4.w, ph_[j + 1], pl[j + 1]);
+                    }
+                    if (tid < CS) ecl[(n & 1) * CS + tid] = reinterpret_cast<const float*>(smem + sp + A_EC)[tid];
+                    ptx::tc_fence_before();
+                    csync();  // all of cols [0,128) read before they are overwritten; e^c copied
+                    ptx::tc_fence_after();
+                    ptx::tmem_st16(tl + T_VN_HI + 16 * half, vh);
+                    ptx::tmem_st16(tl + T_VN_LO + 16 * half, vl);
+                    ptx::tmem_st16(tl + T_VP_HI + 16 * half, ph_);
+                    ptx::tmem_st16(tl + T_VP_LO + 16 * half, pl);
+                    ptx::tmem_wait_st();
+                    hand_off(B_VNR);
                 }
+
+                // ---- S <- e^{cL} S + dS; the new S^T hi/lo operand (S^T q^T has read the old one)
+                wait_bar(B_X1, ph);
+                ptx::tc_fence_after();
+                {
+                    const float gam = ecn[CS - 1];
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    const uint32_t sa = part ? T_SA_LO : T_SA_HI;
+                    for (int c2 = 0; c2 < 2; ++c2) {
+                        float v[32];
+                        ptx::tmem_ld32(tl + T_S + 64 * half + 32 * c2, v);
+                        ptx::tmem_wait_ld();
 #pragma unroll
-                    for (int s = 0; s < 8; ++s) {
-                        const uint64_t b = ptx::sw128_desc(sb + sp + SL_W + s * 2048, 16384, 1024);
-                        ptx::mma_bf16_ts(tmem + T_V, tmem + sa + 8 * s, b, ID_WS, 1u);
+                        for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
                     }
                 }
-                commit();
-            }
-            wait_mma();
-            if (tid == 0 && n + 1 < NC) load_v(n + 1);
-            {   // v_new hi/lo and (v_new e^{cL-c}) hi/lo -> TMEM A operands
-                float v[32];
+                if (n + 1 < NC) {
+                    store_state_operand();
+                    ptx::tmem_wait_st();
+                    hand_off(B_SOP);
+                }
+
+                // ---- o = scale e^c o1 + o2 -> bf16 staging buffer (chunk parity) -> output CTA.
+                //      Staged transposed, o^T [128 dv][64 tok] with 128-byte rows in 16-byte chunks
+                //      XOR-swizzled by (dv & 7): one thread writes its row half with four 16-byte stores.
+                wait_bar(B_Y, ph);
+                ptx::tc_fence_after();
                 {
-                    float v2[32];
-                    ptx::tmem_ld32(tl + T_V + 32 * half, v);
-                    ptx::tmem_ld32(tl + T_V + 64 + 32 * half, v2);
+                    float v[32], v2[32];
+                    ptx::tmem_ld32(tl + T_O + 32 * half, v);
+                    ptx::tmem_ld32(tl + T_O2 + 32 * half, v2);
+                    ptx::tmem_wait_ld();
+                    hand_off(B_OFREE);
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) v[jj] = fmaf(p.scale * ecn[32 * half + jj], v[jj], v2[jj]);
+                    // the output CTA has handed back this buffer (its chunk n - 2)
+                    if (n >= 2 && !ptx::mbar_wait(bar(B_EMPTYO + (n & 1)), (uint32_t)(((n >> 1) - 1) & 1), WAIT_ITERS))
+                        fail();
+                    const uint32_t ob = sb + C_OST + (uint32_t)(n & 1) * O_BYTES;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        st_shared_v4(ob + sw_chunk(row, 4 * half + c, 128), pack_bf16(v[8 * c], v[8 * c + 1]),
+                                     pack_bf16(v[8 * c + 2], v[8 * c + 3]), pack_bf16(v[8 * c + 4], v[8 * c + 5]),
+                                     pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+                }
+                ptx::fence_proxy_async_smem();  // the staging buffer is read by a bulk copy
+                csync();
+                if (tid == 0) {
+                    const uint32_t dst = ptx::mapa(sb + U_OSLOT + (uint32_t)(n & 1) * O_BYTES, OUT_RANK);
+                    const uint32_t fb = ptx::mapa(sb + U_MISC + M_BAR + 8u * (uint32_t)(B_FULLO + (n & 1)), OUT_RANK);
+                    ptx::bulk_copy_s2cluster(dst, sb + C_OST + (uint32_t)(n & 1) * O_BYTES, O_BYTES, fb);
+                }
+            }
+            if (!*abort_flag) {
+                const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
+#pragma unroll
+                for (int j = 0; j < 64; ++j) p.sf[sbase + (size_t)(64 * half + j) * HD + row] = S[j];
+            }
+        } else if (!outcta) {
+            // ---------------- prep CTA
+            const int pi = (int)rank - 1;  // owns chunks pi, pi + NP, ...
+            float* Ls = reinterpret_cast<float*>(smem + P_L);
+            float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
+            // Gates of a later chunk, loaded unconditionally (positions past the sequence end
+            // are clamped to its last token) and masked where they are used, so that nothing
+            // waits on these loads before that chunk.
+            auto load_gates = [&](int n) {
+                const int last = len - n * CS - 1;
+                const long long t0 = tok_base + (long long)n * CS;
+                const int i0 = min(2 * lane, last), i1 = min(2 * lane + 1, last);
+                gn0 = ldg_early(p.g + (size_t)(t0 + i0) * p.HV + h);
+                bn0 = ldg_early(p.beta + (size_t)(t0 + i0) * p.HV + h);
+                gn1 = ldg_early(p.g + (size_t)(t0 + i1) * p.HV + h);
+                bn1 = ldg_early(p.beta + (size_t)(t0 + i1) * p.HV + h);
+            };
+            if (tid == 0 && pi < NC) {
+                load_q(pi);
+                load_k(pi);
+            }
+            if (warp == 0 && pi < NC) load_gates(pi);
+
+            int k = 0;
+            for (int n = pi; n < NC; n += NP, ++k) {
+                const uint32_t stg = P_STG + (uint32_t)(k & 1) * SLOT;
+                float* ec_s = reinterpret_cast<float*>(smem + stg + SL_EC);
+                float* ed_s = reinterpret_cast<float*>(smem + stg + SL_ED);
+                float* X = reinterpret_cast<float*>(smem + stg + SL_W);  // inversion scratch (W area not yet written)
+                const uint32_t ph = (uint32_t)(k & 1);
+                // thread 0 has confirmed that staging[k & 1] was shipped and consumed; every
+                // thread takes the same exit decision
+                if (vote_abort()) break;
+
+                if (warp == 0) {
+                    const int valid = min(CS, len - n * CS);
+                    const bool v0 = 2 * lane < valid, v1 = 2 * lane + 1 < valid;
+                    const float g0 = v0 ? gn0 : 0.f, g1 = v1 ? gn1 : 0.f, b0 = v0 ? bn0 : 0.f, b1 = v1 ? bn1 : 0.f;
+                    if (n + NP < NC) load_gates(n + NP);
+                    float s = g0 + g1;
+#pragma unroll
+                    for (int off = 1; off < 32; off <<= 1) {
+                        const float t = __shfl_up_sync(0xffffffffu, s, off);
+                        if (lane >= off) s += t;
+                    }
+                    const float c1 = s, c0 = s - g1;
+                    const float cL = __shfl_sync(0xffffffffu, c1, 31);
+                    c_s[2 * lane] = c0;
+                    c_s[2 * lane + 1] = c1;
+                    beta_s[2 * lane] = b0;
+                    beta_s[2 * lane + 1] = b1;
+                    ec_s[2 * lane] = ex2f(c0 * LOG2E);
+                    ec_s[2 * lane + 1] = ex2f(c1 * LOG2E);
+                    ed_s[2 * lane] = ex2f((cL - c0) * LOG2E);
+                    ed_s[2 * lane + 1] = ex2f((cL - c1) * LOG2E);
+                }
+                csync();  // warps 1-7 wait here rather than polling the q / k barriers meanwhile
+                wait_bar(B_Q, ph);
+                wait_bar(B_K, ph);
+                if (tid == 0) {
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int s = 0; s < 8; ++s) {
+                        const uint32_t koff = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
+                        const uint64_t a = ptx::sw128_desc(sb + P_QK + koff, 16, 1024);
+                        const uint64_t b = ptx::sw128_desc(sb + P_QK + 8192 + koff, 16, 1024);
+                        ptx::mma_bf16(tmem + T_P, a, b, ID_P, s > 0);
+                    }
+                    commit();
+                }
+                csync();
+                wait_mma();
+                if (tid == 0 && n + NP < NC) load_q(n + NP);  // P1 has read q
+                {   // rows 0-63: M (hi/lo -> staging); rows 64-127: L
+                    float v[32];
+                    ptx::tmem_ld32(tl + T_P + 32 * half, v);
+                    ptx::tmem_wait_ld();
+                    if (row < CS) {
+                        const int i = row;
+                        const float ci = c_s[i];
+                        float m[32];
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) {
+                            const int j = 32 * half + jj;
+                            m[jj] = (j <= i) ? v[jj] * p.scale * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                        }
+#pragma unroll
+                        for (int ch = 0; ch < 4; ++ch) {
+                            const uint32_t co = sw_chunk(i, 4 * half + ch, 64);
+                            put8_split(sb + stg + SL_M + co, sb + stg + SL_M + 8192 + co, m + 8 * ch, true);
+                        }
+                    } else {
+                        const int i = row - CS;
+                        const float ci = c_s[i], bi = beta_s[i];
+                        float* lrow = Ls + i * LSTRIDE + 32 * half;
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; ++j4) {
+                            float4 o4;
+                            float* o = reinterpret_cast<float*>(&o4);
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int jj = 4 * j4 + u, j = 32 * half + jj;
+                                o[u] = (j < i) ? bi * v[jj] * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                            }
+                            *reinterpret_cast<float4*>(lrow + 4 * j4) = o4;
+                        }
+                    }
+                }
+                ptx::tc_fence_before();
+                csync();
+                invert_unit_lower(Ls, X, tid, [](int) {}, csync);
+                {   // T' -> staging (stacked hi/lo), T'' -> local
+                    const int i = tid >> 2, jb = tid & 3;
+                    float tp[16], tpp[16];
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const float4 t4 = ld4(Ls + i * LSTRIDE + 16 * jb + 4 * q4);
+                        const float tt[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int jj = 4 * q4 + u, j = 16 * jb + jj;
+                            tp[jj] = tt[u] * beta_s[j];
+                            tpp[jj] = tp[jj] * ec_s[j];
+                        }
+                    }
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const uint32_t co = sw_chunk(i, 2 * jb + hh, 64);
+                        put8_split(sb + stg + SL_TP + co, sb + stg + SL_TP + 8192 + co, tp + 8 * hh, true);
+                        put8_split(sb + P_TPP + co, sb + P_TPP + 8192 + co, tpp + 8 * hh, true);
+                    }
+                }
+                ptx::fence_proxy_async_smem();
+                csync();
+                if (tid == 0) {  // P3: W^T = K^T [T''_hi; T''_lo]^T
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        const uint64_t a = ptx::sw128_desc(sb + P_QK + 8192 + s * 2048, 16384, 1024);
+                        const uint64_t b = ptx::sw128_desc(sb + P_TPP + s * 32, 16, 1024);
+                        ptx::mma_bf16(tmem + T_W, a, b, ID_W, s > 0);
+                    }
+                    commit();
+                }
+                wait_mma();
+                if (tid == 0 && n + NP < NC) {  // k consumed: fetch this CTA's next chunk
+                    load_k(n + NP);
+                    prefetch_tile(&p.tm_q, hq, n + 2 * NP);
+                    prefetch_tile(&p.tm_k, hq, n + 2 * NP);
+                }
+                {   // W^T rows (dk = row) -> staging, hi and lo tiles 16 KB apart
+                    float v[32], v2[32];
+                    ptx::tmem_ld32(tl + T_W + 32 * half, v);
+                    ptx::tmem_ld32(tl + T_W + 64 + 32 * half, v2);
                     ptx::tmem_wait_ld();
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
-                }
-                uint32_t vh[16], vl[16], ph_[16], pl[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    split2(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
-                    split2(v[2 * j] * ed_s[32 * half + 2 * j], v[2 * j + 1] * ed_s[32 * half + 2 * j + 1], ph_[j], pl[j]);
+                    for (int ch = 0; ch < 4; ++ch) {
+                        const uint32_t co = sw_chunk(row, 4 * half + ch, 128);
+                        put8_split(sb + stg + SL_W + co, sb + stg + SL_W + 16384 + co, v + 8 * ch, true);
+                    }
                 }
                 ptx::tc_fence_before();
-                __syncthreads();  // all of cols [0,128) read before they are overwritten
-                ptx::tc_fence_after();
-                ptx::tmem_st16(tl + T_VN_HI + 16 * half, vh);
-                ptx::tmem_st16(tl + T_VN_LO + 16 * half, vl);
-                ptx::tmem_st16(tl + T_VP_HI + 16 * half, ph_);
-                ptx::tmem_st16(tl + T_VP_LO + 16 * half, pl);
-                ptx::tmem_wait_st();
+                ptx::fence_proxy_async_smem();
+                csync();
+                if (tid == 0) {  // ship each part once the chain has handed back that part of the previous chunk
+                    auto wait_empty = [&](int b) {
+                        if (ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) ++consumed[b];
+                        else fail();
+                    };
+                    // the chain CTA's slots and barriers sit at its own offsets
+                    const uint32_t fa = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLA + pi), 0);
+                    const uint32_t fbb = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLB + pi), 0);
+                    const uint32_t da = ptx::mapa(sb + C_ASLOT + (uint32_t)pi * ASLOT, 0);
+                    const uint32_t db = ptx::mapa(sb + C_BSLOT + (uint32_t)pi * B_BYTES, 0);
+                    if (k >= 1) wait_empty(B_EMPTYA);
+                    ptx::bulk_copy_s2cluster(da + A_TP, sb + stg + SL_TP, SL_M - SL_TP, fa);
+                    ptx::bulk_copy_s2cluster(da + A_EC, sb + stg + SL_EC, 512, fa);
+                    if (k >= 1) wait_empty(B_EMPTYB);
+                    ptx::bulk_copy_s2cluster(db, sb + stg + SL_M, B_BYTES, fbb);
+                }
             }
-            ptx::tc_fence_before();
-            __syncthreads();
-            if (*abort_flag) break;
-
-            // ---- C3 / C4
-            wait_bar(B_Q, ph);
-            wait_bar(B_K, ph);
-            if (tid == 0) {
-                ptx::tc_fence_after();
+            if (tid == 0 && k >= 1 && !*abort_flag) {  // the last shipment must land before this CTA exits
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    const uint32_t sa = part ? T_SA_LO : T_SA_HI;
+                for (int b = B_EMPTYA; b <= B_EMPTYB; ++b) {
+                    if (ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) ++consumed[b];
+                    else fail();
+                }
+            }
+        } else {
+            // ---------------- output CTA: gated-RMSNorm epilogue of every chunk (4 threads per
+            // token, 16-byte chunks {eq, eq+4, eq+8, eq+12}); o arrives from the chain CTA
+            const int et = tid >> 2, eq = tid & 3;
+            auto load_zt = [&](int n) { load_tile(B_ZT + (n & 1), U_Z + (uint32_t)(n & 1) * O_BYTES, &p.tm_z, h, n); };
+            if (tid == 0 && p.gated)
+                for (int s = 0; s < 2 && s < NC; ++s) load_zt(s);
+            for (int n = 0; n < NC; ++n) {
+                if (vote_abort()) break;
+                const int valid = min(CS, len - n * CS);
+                const long long tok0 = tok_base + (long long)n * CS;
+                const uint32_t par = (uint32_t)((n >> 1) & 1);
+                const uint32_t oslot = U_OSLOT + (uint32_t)(n & 1) * O_BYTES;
+                const uint32_t zt = U_Z + (uint32_t)(n & 1) * O_BYTES;
+                wait_bar(B_FULLO + (n & 1), par);
+                {   // o^T -> o: thread (dv, token half) reads four 16-byte chunks of row dv
+                    const int dv = tid >> 1, th = tid & 1;
+                    __nv_bfloat16* ot = reinterpret_cast<__nv_bfloat16*>(smem + U_OT);
 #pragma unroll
-                    for (int s = 0; s < 8; ++s) {
-                        const uint64_t b =
-                            ptx::sw128_desc(sb + C_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
-                        ptx::mma_bf16_ts(tmem + T_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t w4[4];
+                        ld_shared_v4(sb + oslot + sw_chunk(dv, 4 * th + c, 128), w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
+                            const int t = 32 * th + 8 * c + 2 * u;
+                            ot[sw_off(t, dv, 64) >> 1] = b2.x;
+                            ot[sw_off(t + 1, dv, 64) >> 1] = b2.y;
+                        }
                     }
                 }
-#pragma unroll
-                for (int term = 0; term < 3; ++term) {
-                    const uint32_t va = (term == 1) ? T_VN_LO : T_VN_HI;
-                    const uint32_t mb = sp + SL_M + ((term == 2) ? 8192u : 0u);
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        const uint64_t b = ptx::sw128_desc(sb + mb + s * 32, 16, 1024);
-                        ptx::mma_bf16_ts(tmem + T_O2, tmem + va + 8 * s, b, ID_O, (term | s) > 0);
+                csync();  // o slot read, o staged
+                if (tid == 0) {
+                    if (n + 2 < NC) {  // this parity's slot takes chunk n + 2
+                        ++issued[B_FULLO + (n & 1)];
+                        ptx::mbar_arrive_expect_tx(bar(B_FULLO + (n & 1)), O_BYTES);
                     }
+                    // the chain CTA's barriers sit at its own misc offset
+                    ptx::mbar_arrive_remote(ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_EMPTYO + (n & 1)), 0));
                 }
-#pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    const uint32_t va = part ? T_VP_LO : T_VP_HI;
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        const uint64_t b = ptx::sw128_desc(sb + C_QK + 8192 + s * 2048, 16384, 1024);
-                        ptx::mma_bf16_ts(tmem + T_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
-                    }
-                }
-                commit();
-            }
-            wait_mma();
-            if (tid == 0 && n + 1 < NC) {
-                load_q(n + 1);
-                load_k(n + 1);
-            }
-            {   // S <- e^{cL} S + dS
-                const float gam = ec_s[CS - 1];
-#pragma unroll
-                for (int c2 = 0; c2 < 2; ++c2) {
-                    float v[32];
-                    ptx::tmem_ld32(tl + T_S + 64 * half + 32 * c2, v);
-                    ptx::tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
-                }
-            }
-            {   // o = scale e^c o1 + o2 -> bf16 staging
-                float v[32], v2[32];
-                ptx::tmem_ld32(tl + T_O + 32 * half, v);
-                ptx::tmem_ld32(tl + T_O2 + 32 * half, v2);
-                ptx::tmem_wait_ld();
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) v[jj] = fmaf(p.scale * ec_s[32 * half + jj], v[jj], v2[jj]);
-                __nv_bfloat16* ot = reinterpret_cast<__nv_bfloat16*>(smem + C_OST);
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) ot[sw_off(32 * half + jj, row, 64) >> 1] = __float2bfloat16_rn(v[jj]);
-            }
-            store_state_operand();
-            ptx::tmem_wait_st();
-            ptx::tc_fence_before();
-            __syncthreads();  // slot fully consumed, o staged, new S operand in TMEM
-            if (tid == 0) {   // hand the slot back to its prep CTA
-                if (n + NP < NC) {
-                    ++issued[B_FULL + slot];
-                    ptx::mbar_arrive_expect_tx(bar(B_FULL + slot), SL_BYTES);
-                }
-                // the prep CTA's barriers sit at its own misc offset
-                ptx::mbar_arrive_remote(ptx::mapa(sb + P_MISC + M_BAR + 8u * B_EMPTY, (uint32_t)(1 + slot)));
-            }
-
-            // ---- epilogue: 4 threads per token, 16-byte chunks {eq, eq+4, eq+8, eq+12}
-            {
                 float o[32];
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
                     uint32_t w4[4];
-                    ld_shared_v4(sb + C_OST + sw_chunk(et, eq + 4 * m, 64), w4[0], w4[1], w4[2], w4[3]);
+                    ld_shared_v4(sb + U_OT + sw_chunk(et, eq + 4 * m, 64), w4[0], w4[1], w4[2], w4[3]);
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
@@ -366,12 +629,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
                     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
                     const float rstd = rsqrtf(ss * (1.f / (float)HD) + p.eps);
-                    wait_bar(B_Z, ph);
+                    wait_bar(B_ZT + (n & 1), par);
 #pragma unroll
                     for (int m = 0; m < 4; ++m) {
                         const int c = eq + 4 * m;
                         uint32_t w4[4];
-                        ld_shared_v4(sb + C_Z + sw_chunk(et, c, 64), w4[0], w4[1], w4[2], w4[3]);
+                        ld_shared_v4(sb + zt + sw_chunk(et, c, 64), w4[0], w4[1], w4[2], w4[3]);
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
                             const int j = 8 * m + 2 * u, dv = 8 * c + 2 * u;
@@ -390,208 +653,193 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     for (int m = 0; m < 4; ++m)
                         dst[eq + 4 * m] = make_uint4(outw[4 * m], outw[4 * m + 1], outw[4 * m + 2], outw[4 * m + 3]);
                 }
+                csync();  // o and z tile read
+                if (tid == 0 && p.gated && n + 2 < NC) {  // this parity's z tile takes chunk n + 2
+                    ptx::fence_proxy_async_smem();
+                    load_zt(n + 2);
+                    prefetch_tile(&p.tm_z, h, n + 3);
+                }
             }
-            __syncthreads();
-            if (tid == 0 && p.gated && n + 1 < NC) {
-                ptx::fence_proxy_async_smem();
-                load_z(n + 1);
-            }
+            // Abort path: wait (bounded) for the z loads and the chain's o copies armed here
+            if (*abort_flag && tid == 0)
+                for (int i = B_FULLO; i < B_ZT + 2; ++i)
+                    while (consumed[i] < issued[i]) {
+                        ptx::mbar_wait(bar(i), consumed[i] & 1u, WAIT_ITERS);
+                        ++consumed[i];
+                    }
         }
-        if (!*abort_flag) {
-            const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
-#pragma unroll
-            for (int j = 0; j < 64; ++j) p.sf[sbase + (size_t)(64 * half + j) * HD + row] = S[j];
+        // Abort path: wait (bounded) for the TMA loads and MMAs this thread issued before
+        // the shared memory and TMEM are released.
+        if (*abort_flag && tid == 0 && !outcta) {
+            for (int i = B_Q; i <= B_K; ++i)
+                while (consumed[i] < issued[i]) {
+                    ptx::mbar_wait(bar(i), consumed[i] & 1u, WAIT_ITERS);
+                    ++consumed[i];
+                }
+            if (!chain)
+                while (consumed[B_MMA] < issued[B_MMA]) {
+                    ptx::mbar_wait(bar(B_MMA), consumed[B_MMA] & 1u, WAIT_ITERS);
+                    ++consumed[B_MMA];
+                }
         }
+        csync();
+        if (tid == 0) *done_flag = 1;  // lets the idle warps of warpgroup 2 stop sleeping
     } else {
-        // ============================== prep CTA ==============================
-        const int pi = (int)rank - 1;  // owns chunks pi, pi + NP, ...
-        float* Ls = reinterpret_cast<float*>(smem + P_L);
-        float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
-        auto load_gates = [&](int n) {
-            const int valid = min(CS, len - n * CS);
-            const long long t0 = tok_base + (long long)n * CS;
-            gn0 = gn1 = bn0 = bn1 = 0.f;
-            if (2 * lane < valid) {
-                gn0 = __ldg(p.g + (size_t)(t0 + 2 * lane) * p.HV + h);
-                bn0 = __ldg(p.beta + (size_t)(t0 + 2 * lane) * p.HV + h);
-            }
-            if (2 * lane + 1 < valid) {
-                gn1 = __ldg(p.g + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
-                bn1 = __ldg(p.beta + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
-            }
+        // ============================== warpgroup 2 ==============================
+        ptx::setmaxnreg_dec<ISSUE_REGS>();
+        const bool mma_warp = chain && warp == ISSUER_WARP;
+        const bool producer = chain && warp == ISSUER_WARP + 1;
+        auto prep_bar = [&](int b, int m) {  // the prep CTAs' barriers sit at their own misc offset
+            return ptx::mapa(sb + P_MISC + M_BAR + 8u * (uint32_t)b, (uint32_t)(1 + m % NSLOT));
         };
-        ptx::cluster_sync();
-        if (tid == 0 && pi < NC) {
-            load_q(pi);
-            load_k(pi);
+        auto arm_slot = [&](int b, int m, uint32_t bytes) {
+            ++issued[b + m % NSLOT];
+            ptx::mbar_arrive_expect_tx(bar(b + m % NSLOT), bytes);
+        };
+        if (producer && lane == 0) {  // arm the slots for each prep CTA's first chunk
+            for (int s = 0; s < NSLOT && s < NC; ++s) {
+                arm_slot(B_FULLA, s, A_BYTES);
+                arm_slot(B_FULLB, s, B_BYTES);
+            }
         }
-        if (warp == 0 && pi < NC) load_gates(pi);
+        __syncwarp();
+        ptx::tc_fence_before();
+        ptx::cluster_sync();  // every CTA's barriers are initialised and the slots armed
+        ptx::tc_fence_after();
 
-        int k = 0;
-        for (int n = pi; n < NC; n += NP, ++k) {
-            if (*abort_flag) break;
-            const uint32_t stg = P_STG + (uint32_t)(k & 1) * SLOT;
-            float* ec_s = reinterpret_cast<float*>(smem + stg + SL_EC);
-            float* ed_s = reinterpret_cast<float*>(smem + stg + SL_ED);
-            float* X = reinterpret_cast<float*>(smem + stg + SL_W);  // inversion scratch (W area not yet written)
-            const uint32_t ph = (uint32_t)(k & 1);
-            __syncthreads();  // thread 0 has confirmed that staging[k & 1] was shipped and consumed
-
-            if (warp == 0) {
-                const float g0 = gn0, g1 = gn1, b0 = bn0, b1 = bn1;
-                if (n + NP < NC) load_gates(n + NP);
-                float s = g0 + g1;
+        if (mma_warp) {
+            // ---------------- MMA issue. tcgen05.mma occupies the issuing thread for about the
+            // instruction's execution time, so this warp issues MMAs and waits only on what
+            // gates them; loads and slot hand-backs run on the producer warp.
+            auto wait_full = [&](int b, int m) {
+                if (ptx::mbar_wait(bar(b + m % NSLOT), slot_par(m), WAIT_ITERS)) ++consumed[b + m % NSLOT];
+                else fail();
+            };
+            if (lane == 0) {
+                for (int n = 0; n < NC; ++n) {
+                    if (*abort_flag) break;
+                    const uint32_t ph = (uint32_t)(n & 1);
+                    const uint32_t sp = aslot(n);
+                    // ---- C12: v_new^T = v^T [T'_hi;T'_lo]^T - S^T [W_hi|W_lo] (hi terms cols 0-63, lo 64-127);
+                    //      the v^T T'^T part does not depend on the state and goes first
+                    wait_full(B_FULLA, n);
+                    wait_bar(B_V, ph);
+                    if (n > 0) wait_bar(B_Y, (uint32_t)((n - 1) & 1));  // v_new operands of chunk n-1 read
+                    ptx::tc_fence_after();
 #pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const float t = __shfl_up_sync(0xffffffffu, s, off);
-                    if (lane >= off) s += t;
-                }
-                const float c1 = s, c0 = s - g1;
-                const float cL = __shfl_sync(0xffffffffu, c1, 31);
-                c_s[2 * lane] = c0;
-                c_s[2 * lane + 1] = c1;
-                beta_s[2 * lane] = b0;
-                beta_s[2 * lane + 1] = b1;
-                ec_s[2 * lane] = ex2f(c0 * LOG2E);
-                ec_s[2 * lane + 1] = ex2f(c1 * LOG2E);
-                ed_s[2 * lane] = ex2f((cL - c0) * LOG2E);
-                ed_s[2 * lane + 1] = ex2f((cL - c1) * LOG2E);
-            }
-            wait_bar(B_Q, ph);
-            wait_bar(B_K, ph);
-            if (tid == 0) {
-                ptx::tc_fence_after();
-#pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const uint32_t koff = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
-                    const uint64_t a = ptx::sw128_desc(sb + P_QK + koff, 16, 1024);
-                    const uint64_t b = ptx::sw128_desc(sb + P_QK + 8192 + koff, 16, 1024);
-                    ptx::mma_bf16(tmem + T_P, a, b, ID_P, s > 0);
-                }
-                commit();
-            }
-            __syncthreads();
-            wait_mma();
-            {   // rows 0-63: M (hi/lo -> staging); rows 64-127: L
-                float v[32];
-                ptx::tmem_ld32(tl + T_P + 32 * half, v);
-                ptx::tmem_wait_ld();
-                if (row < CS) {
-                    const int i = row;
-                    const float ci = c_s[i];
-                    float m[32];
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) {
-                        const int j = 32 * half + jj;
-                        m[jj] = (j <= i) ? v[jj] * p.scale * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                    for (int s = 0; s < 4; ++s) {
+                        const uint64_t a = ptx::sw128_desc(sb + C_V + s * 2048, 8192, 1024);
+                        const uint64_t b = ptx::sw128_desc(sb + sp + A_TP + s * 32, 16, 1024);
+                        ptx::mma_bf16(tmem + T_V, a, b, ID_U, s > 0);
                     }
+                    commit_to(B_VT);      // the v tile is free once these have run
+                    wait_bar(B_SOP, ph);  // S_n^T hi/lo in TMEM
+                    ptx::tc_fence_after();
 #pragma unroll
-                    for (int ch = 0; ch < 4; ++ch) {
-                        const uint32_t co = sw_chunk(i, 4 * half + ch, 64);
-                        put8_split(sb + stg + SL_M + co, sb + stg + SL_M + 8192 + co, m + 8 * ch, true);
-                    }
-                } else {
-                    const int i = row - CS;
-                    const float ci = c_s[i], bi = beta_s[i];
-                    float* lrow = Ls + i * LSTRIDE + 32 * half;
+                    for (int part = 0; part < 2; ++part) {
+                        const uint32_t sa = part ? T_SA_LO : T_SA_HI;
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        float4 o4;
-                        float* o = reinterpret_cast<float*>(&o4);
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int jj = 4 * j4 + u, j = 32 * half + jj;
-                            o[u] = (j < i) ? bi * v[jj] * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                        for (int s = 0; s < 8; ++s) {
+                            const uint64_t b = ptx::sw128_desc(sb + sp + A_W + s * 2048, 16384, 1024);
+                            ptx::mma_bf16_ts(tmem + T_V, tmem + sa + 8 * s, b, ID_WS, 1u);
                         }
-                        *reinterpret_cast<float4*>(lrow + 4 * j4) = o4;
                     }
-                }
-            }
-            ptx::tc_fence_before();
-            __syncthreads();
-            invert_unit_lower(Ls, X, tid, [](int) {});
-            {   // T' -> staging (stacked hi/lo), T'' -> local
-                const int i = tid >> 2, jb = tid & 3;
-                float tp[16], tpp[16];
+                    commit();
+                    // ---- o1^T = S^T q^T, once the previous chunk's output accumulators are read
+                    wait_bar(B_Q, ph);
+                    if (n > 0) wait_bar(B_OFREE, (uint32_t)((n - 1) & 1));
+                    ptx::tc_fence_after();
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const float4 t4 = ld4(Ls + i * LSTRIDE + 16 * jb + 4 * q4);
-                    const float tt[4] = {t4.x, t4.y, t4.z, t4.w};
+                    for (int part = 0; part < 2; ++part) {
+                        const uint32_t sa = part ? T_SA_LO : T_SA_HI;
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int jj = 4 * q4 + u, j = 16 * jb + jj;
-                        tp[jj] = tt[u] * beta_s[j];
-                        tpp[jj] = tp[jj] * ec_s[j];
+                        for (int s = 0; s < 8; ++s) {
+                            const uint64_t b = ptx::sw128_desc(sb + C_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
+                            ptx::mma_bf16_ts(tmem + T_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
+                        }
                     }
-                }
+                    // ---- dS^T = (v_new e^{cL-c})^T K, o2^T = v_new^T M^T, once v_new is in TMEM
+                    wait_bar(B_K, ph);
+                    wait_full(B_FULLB, n);
+                    wait_bar(B_VNR, ph);
+                    ptx::tc_fence_after();
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const uint32_t co = sw_chunk(i, 2 * jb + hh, 64);
-                    put8_split(sb + stg + SL_TP + co, sb + stg + SL_TP + 8192 + co, tp + 8 * hh, true);
-                    put8_split(sb + P_TPP + co, sb + P_TPP + 8192 + co, tpp + 8 * hh, true);
-                }
-            }
-            ptx::fence_proxy_async_smem();
-            __syncthreads();
-            if (tid == 0) {  // P3: W^T = K^T [T''_hi; T''_lo]^T
-                ptx::tc_fence_after();
+                    for (int part = 0; part < 2; ++part) {
+                        const uint32_t va = part ? T_VP_LO : T_VP_HI;
 #pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint64_t a = ptx::sw128_desc(sb + P_QK + 8192 + s * 2048, 16384, 1024);
-                    const uint64_t b = ptx::sw128_desc(sb + P_TPP + s * 32, 16, 1024);
-                    ptx::mma_bf16(tmem + T_W, a, b, ID_W, s > 0);
-                }
-                commit();
-            }
-            wait_mma();
-            if (tid == 0 && n + NP < NC) {  // q and k consumed: fetch this CTA's next chunk
-                load_q(n + NP);
-                load_k(n + NP);
-            }
-            {   // W^T rows (dk = row) -> staging, hi and lo tiles 16 KB apart
-                float v[32], v2[32];
-                ptx::tmem_ld32(tl + T_W + 32 * half, v);
-                ptx::tmem_ld32(tl + T_W + 64 + 32 * half, v2);
-                ptx::tmem_wait_ld();
+                        for (int s = 0; s < 4; ++s) {
+                            const uint64_t b = ptx::sw128_desc(sb + C_QK + 8192 + s * 2048, 16384, 1024);
+                            ptx::mma_bf16_ts(tmem + T_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
+                        }
+                    }
+                    commit_to(B_X1);
+                    const uint32_t bp = bslot(n);
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
+                    for (int term = 0; term < 3; ++term) {
+                        const uint32_t va = (term == 1) ? T_VN_LO : T_VN_HI;
+                        const uint32_t mb = bp + ((term == 2) ? 8192u : 0u);
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    const uint32_t co = sw_chunk(row, 4 * half + ch, 128);
-                    put8_split(sb + stg + SL_W + co, sb + stg + SL_W + 16384 + co, v + 8 * ch, true);
+                        for (int s = 0; s < 4; ++s) {
+                            const uint64_t b = ptx::sw128_desc(sb + mb + s * 32, 16, 1024);
+                            ptx::mma_bf16_ts(tmem + T_O2, tmem + va + 8 * s, b, ID_O, (term | s) > 0);
+                        }
+                    }
+                    commit_to(B_Y);
+                }
+                if (*abort_flag) {  // wait (bounded) for every MMA this thread issued
+                    commit_to(B_DRAIN);
+                    ptx::mbar_wait(bar(B_DRAIN), 0u, WAIT_ITERS);
                 }
             }
-            ptx::tc_fence_before();
-            ptx::fence_proxy_async_smem();
-            __syncthreads();
-            if (tid == 0) {  // ship to the chain CTA once it has consumed this CTA's previous chunk
-                if (k >= 1) {
-                    if (ptx::mbar_wait_cluster(bar(B_EMPTY), (uint32_t)((k - 1) & 1), WAIT_ITERS)) ++consumed[B_EMPTY];
-                    else fail();
+            __syncwarp();
+        } else if (producer) {
+            // ---------------- TMA loads and slot hand-backs, each as soon as its buffer is free
+            if (lane == 0 && NC > 0) {
+                load_q(0);
+                load_k(0);
+                load_v(0);
+                for (int n = 0; n < NC; ++n) {
+                    if (*abort_flag) break;
+                    const uint32_t ph = (uint32_t)(n & 1);
+                    wait_bar(B_VT, ph);  // v^T T'^T has read the v tile
+                    if (n + 1 < NC) load_v(n + 1);
+                    prefetch_tile(&p.tm_v, h, n + 2);
+                    wait_bar(B_VNR, ph);  // C12 read part A; decay factors copied
+                    if (n + NSLOT < NC) arm_slot(B_FULLA, n, A_BYTES);
+                    ptx::mbar_arrive_remote(prep_bar(B_EMPTYA, n));
+                    wait_bar(B_X1, ph);  // S^T q^T and dS done: q and k tiles free
+                    if (n + 1 < NC) {
+                        load_q(n + 1);
+                        load_k(n + 1);
+                    }
+                    prefetch_tile(&p.tm_q, hq, n + 2);
+                    prefetch_tile(&p.tm_k, hq, n + 2);
+                    wait_bar(B_Y, ph);  // v_new^T M^T done: part B free
+                    if (n + NSLOT < NC) arm_slot(B_FULLB, n, B_BYTES);
+                    ptx::mbar_arrive_remote(prep_bar(B_EMPTYB, n));
                 }
-                const uint32_t dst = ptx::mapa(sb + C_SLOT + (uint32_t)pi * SLOT, 0);
-                const uint32_t fb = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULL + pi), 0);
-                ptx::bulk_copy_s2cluster(dst, sb + stg, 65536, fb);
-                ptx::bulk_copy_s2cluster(dst + 65536, sb + stg + 65536, SL_BYTES - 65536, fb);
+                if (*abort_flag) {
+                    // wait (bounded) for the last phase armed on each TMA tile and slot barrier:
+                    // a barrier is re-armed only after its previous phase was consumed
+                    for (int i = B_Q; i <= B_V; ++i)
+                        if (issued[i] > 0) ptx::mbar_wait(bar(i), (issued[i] - 1) & 1u, WAIT_ITERS);
+                    for (int i = B_FULLA; i < NBAR; ++i)
+                        if (issued[i] > 0) ptx::mbar_wait(bar(i), (issued[i] - 1) & 1u, WAIT_ITERS);
+                }
             }
+            __syncwarp();
+        } else {
+            // Idle warps sleep until warps 0-7 are done instead of waiting at the cluster
+            // barrier for the whole kernel, where they would take issue slots from the
+            // working warps of this SM. Bounded; the barrier below is what synchronises.
+            if (lane == 0)
+                for (uint32_t it = 0; it < (1u << 21) && *done_flag == 0; ++it) __nanosleep(1000);
+            __syncwarp();
         }
-        if (tid == 0 && k >= 1 && !*abort_flag) {  // the last shipment must land before this CTA exits
-            if (ptx::mbar_wait_cluster(bar(B_EMPTY), (uint32_t)((k - 1) & 1), WAIT_ITERS)) ++consumed[B_EMPTY];
-            else fail();
-        }
-    }
-
-    if (*abort_flag && tid == 0) {
-#pragma unroll
-        for (int i = 0; i < 5; ++i)
-            while (consumed[i] < issued[i]) {
-                ptx::mbar_wait(bar(i), consumed[i] & 1u, WAIT_ITERS);
-                ++consumed[i];
-            }
     }
     ptx::tc_fence_before();
     ptx::cluster_sync();  // no CTA leaves while a peer may still touch its shared memory
-    if (warp == 0) {
+    if (warp == 0 && tmem_cols > 0) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, tmem_cols);
     }
@@ -599,26 +847,50 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
 }  // namespace split
 
+// The kernel's register split (setmaxnreg) assumes exactly LAUNCH_REGS registers per
+// thread at launch; with fewer, the increase in warpgroups 0-1 would never be granted.
+// The compiled count is checked once per device and the kernel is not launched unless
+// it matches.
+static cudaError_t split_prepare(int dev) {
+    static int state[64] = {};  // 0 unchecked, 1 ready, 2 unusable
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (state[dev] == 0) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, split::gdn_prefill_split_kernel);
+        if (e != cudaSuccess) return e;
+        if (fa.numRegs != split::LAUNCH_REGS) {
+            state[dev] = 2;
+        } else {
+            e = cudaFuncSetAttribute(split::gdn_prefill_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)split::SMEM_ALLOC);
+            if (e != cudaSuccess) return e;
+            state[dev] = 1;
+        }
+    }
+    return state[dev] == 1 ? cudaSuccess : cudaErrorNotSupported;
+}
+
+bool split_available() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    return split_prepare(dev) == cudaSuccess;
+}
+
 cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream) {
-    static bool attr_done[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 64 && !attr_done[dev]) {
-        e = cudaFuncSetAttribute(split::gdn_prefill_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)split::SMEM_ALLOC);
-        if (e != cudaSuccess) return e;
-        attr_done[dev] = true;
-    }
+    e = split_prepare(dev);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(1 + split::NP, HV, nseq);
+    cfg.gridDim = dim3(split::CLUSTER, HV, nseq);
     cfg.blockDim = dim3(split::NTHREADS, 1, 1);
     cfg.dynamicSmemBytes = split::SMEM_ALLOC;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1 + split::NP;
+    attr[0].val.clusterDim.x = split::CLUSTER;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
@@ -628,6 +900,6 @@ cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream)
     return cudaGetLastError();
 }
 
-int split_cluster_ctas() { return 1 + split::NP; }
+int split_cluster_ctas() { return split::CLUSTER; }
 
 }  // namespace gdn
