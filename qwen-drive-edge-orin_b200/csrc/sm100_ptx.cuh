@@ -43,8 +43,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: returns false after ~max_iters polls (with backoff).
+// Bounded wait: returns false after ~max_iters polls (with backoff). The poll loop is kept
+// rolled: unrolled at each of the many inlined call sites it multiplies the kernel's code
+// size and the instruction-cache misses that come with it.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t max_iters) {
+#pragma unroll 1
     for (uint32_t it = 0; it < max_iters; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if (it > 64) __nanosleep(64);
