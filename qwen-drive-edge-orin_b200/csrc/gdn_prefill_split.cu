@@ -63,6 +63,7 @@ constexpr uint32_t SL_M = 49152;     // M hi, lo: [64][64] bf16, 8 KB apart
 constexpr uint32_t SL_EC = 65536;    // e^c      [64] f32
 constexpr uint32_t SL_ED = 65792;    // e^{cL-c} [64] f32
 constexpr uint32_t SLOT = 66560;     // staging stride (1024-aligned)
+static_assert(SL_ED == SL_EC + 4 * CS, "e^{cL-c} follows e^c (one copy moves both)");
 // ---- chain CTA slot layout: part A = staging [SL_TP, SL_M) + [SL_EC, SL_EC + 512), part B = M
 constexpr uint32_t A_TP = 0, A_W = 16384, A_EC = 49152, A_ED = 49408;
 constexpr uint32_t A_BYTES = 49664;
@@ -85,7 +86,9 @@ constexpr uint32_t P_QK = 0;
 constexpr uint32_t P_L = 32768;                  // L / T fp32 [64][68]
 constexpr uint32_t P_TPP = 50176;                // T'' hi, lo [64][64] bf16
 constexpr uint32_t P_STG = 66560;                // 2 staging slots
-constexpr uint32_t P_MISC = P_STG + 2 * SLOT;
+constexpr uint32_t P_GATE = P_STG + 2 * SLOT;    // 2 gate slots (chunk parity): c, beta, e^c, e^{cL-c} [64] f32
+constexpr uint32_t GSLOT = 1024;
+constexpr uint32_t P_MISC = P_GATE + 2 * GSLOT;
 // ---- output CTA shared memory
 constexpr uint32_t U_OSLOT = 0;                  // 2 o^T slots (chunk parity), filled by the chain CTA
 constexpr uint32_t U_Z = 2 * O_BYTES;            // 2 z tiles (chunk parity)
@@ -112,10 +115,13 @@ enum {
     B_VNR = 7, B_SOP = 8, B_OFREE = 9, B_VT = 10,
     B_FULLA = 11 /* chain: NSLOT */, B_FULLB = B_FULLA + NSLOT /* chain: NSLOT */,
     B_EMPTYO = B_FULLB + NSLOT /* chain: 2 */,
+    B_X2 = B_EMPTYO + 2 /* chain: S^T q^T done */, B_DRAIN2 = B_X2 + 1 /* chain: output-MMA warp, abort path */,
     B_EMPTYA = 11 /* prep */, B_EMPTYB = 12 /* prep */,
+    B_GREADY = 13 /* prep: 2, gate slot written (32 arrivals) */, B_GFREE = 15 /* prep: 2, gate slot read */,
     B_FULLO = 11 /* output: 2 */, B_ZT = 13 /* output: 2 */
 };
-constexpr int NBAR = B_EMPTYO + 2;
+constexpr int NBAR = B_DRAIN2 + 1;
+static_assert(B_GFREE + 2 <= NBAR, "prep barriers exceed the barrier area");
 static_assert(M_BAR + 8 * NBAR <= M_TMEM, "barriers overlap the TMEM address word");
 
 // ---- TMEM
@@ -157,8 +163,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
     const uint32_t misc_off = chain ? C_MISC : (outcta ? U_MISC : P_MISC);
     float* misc = reinterpret_cast<float*>(smem + misc_off);
-    float* c_s = misc + M_C / 4;
-    float* beta_s = misc + M_BETA / 4;
     float* w_s = misc + M_W / 4;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + misc_off + M_FLAG);
     volatile int* done_flag = reinterpret_cast<volatile int*>(smem + misc_off + M_DONE);
@@ -168,7 +172,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
     if (tid == 0) {
         for (int i = 0; i < NBAR; ++i)
-            ptx::mbar_init(bar(i), (chain && i >= B_VNR && i <= B_OFREE) ? (uint32_t)NCOMPUTE : 1u);
+            ptx::mbar_init(bar(i), (chain && i >= B_VNR && i <= B_OFREE)                      ? (uint32_t)NCOMPUTE
+                                   : (!chain && !outcta && (i == B_GREADY || i == B_GREADY + 1)) ? 32u
+                                                                                               : 1u);
         ptx::fence_mbar_init();
         *abort_flag = 0;
         *done_flag = 0;
@@ -253,23 +259,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 ptx::tmem_st16(tl + T_SA_LO + 32 * half + 16 * c2, lo);
             }
         };
-        if (chain) {  // initial state operand
-            const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                const int dk = 64 * half + j;
-                S[j] = (p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f;
+        if (outcta && tid == 0) {  // arm the o slots for the first two chunks
+            for (int s = 0; s < 2 && s < NC; ++s) {
+                ++issued[B_FULLO + s];
+                ptx::mbar_arrive_expect_tx(bar(B_FULLO + s), O_BYTES);
             }
-            store_state_operand();
-            ptx::tmem_wait_st();
-            hand_off(B_SOP);
-        } else if (outcta) {  // norm weight; arm the o slots for the first two chunks
-            if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;
-            if (tid == 0)
-                for (int s = 0; s < 2 && s < NC; ++s) {
-                    ++issued[B_FULLO + s];
-                    ptx::mbar_arrive_expect_tx(bar(B_FULLO + s), O_BYTES);
-                }
         }
         ptx::tc_fence_before();
         ptx::cluster_sync();  // every CTA's barriers are initialised and the slots armed
@@ -277,6 +271,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
         if (chain) {
             // ---------------- chain CTA: state, operands, output
+            {   // initial state operand (after the cluster barrier: the prep CTAs need not wait for it)
+                const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
+#pragma unroll
+                for (int j = 0; j < 64; ++j) {
+                    const int dk = 64 * half + j;
+                    S[j] = (p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f;
+                }
+                store_state_operand();
+                ptx::tmem_wait_st();
+                hand_off(B_SOP);
+            }
             float* ecl = misc + M_C / 4;  // e^c of chunks with even / odd index (M_C, M_BETA areas)
             for (int n = 0; n < NC; ++n) {
                 if (vote_abort()) break;
@@ -334,6 +339,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
                     }
                 }
+                wait_bar(B_X2, ph);  // S^T q^T has read the old state operand
+                ptx::tc_fence_after();
                 if (n + 1 < NC) {
                     store_state_operand();
                     ptx::tmem_wait_st();
@@ -380,59 +387,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // ---------------- prep CTA
             const int pi = (int)rank - 1;  // owns chunks pi, pi + NP, ...
             float* Ls = reinterpret_cast<float*>(smem + P_L);
-            float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
-            // Gates of a later chunk, loaded unconditionally (positions past the sequence end
-            // are clamped to its last token) and masked where they are used, so that nothing
-            // waits on these loads before that chunk.
-            auto load_gates = [&](int n) {
-                const int last = len - n * CS - 1;
-                const long long t0 = tok_base + (long long)n * CS;
-                const int i0 = min(2 * lane, last), i1 = min(2 * lane + 1, last);
-                gn0 = ldg_early(p.g + (size_t)(t0 + i0) * p.HV + h);
-                bn0 = ldg_early(p.beta + (size_t)(t0 + i0) * p.HV + h);
-                gn1 = ldg_early(p.g + (size_t)(t0 + i1) * p.HV + h);
-                bn1 = ldg_early(p.beta + (size_t)(t0 + i1) * p.HV + h);
-            };
             if (tid == 0 && pi < NC) {
                 load_q(pi);
                 load_k(pi);
             }
-            if (warp == 0 && pi < NC) load_gates(pi);
 
             int k = 0;
             for (int n = pi; n < NC; n += NP, ++k) {
                 const uint32_t stg = P_STG + (uint32_t)(k & 1) * SLOT;
-                float* ec_s = reinterpret_cast<float*>(smem + stg + SL_EC);
-                float* ed_s = reinterpret_cast<float*>(smem + stg + SL_ED);
+                // c, beta, e^c, e^{cL-c} of this chunk, written by the gate warp
+                const float* gs = reinterpret_cast<const float*>(smem + P_GATE + (uint32_t)(k & 1) * GSLOT);
+                const float *c_s = gs, *beta_s = gs + CS, *ec_s = gs + 2 * CS;  // e^{cL-c} follows e^c
                 float* X = reinterpret_cast<float*>(smem + stg + SL_W);  // inversion scratch (W area not yet written)
                 const uint32_t ph = (uint32_t)(k & 1);
                 // thread 0 has confirmed that staging[k & 1] was shipped and consumed; every
                 // thread takes the same exit decision
                 if (vote_abort()) break;
 
-                if (warp == 0) {
-                    const int valid = min(CS, len - n * CS);
-                    const bool v0 = 2 * lane < valid, v1 = 2 * lane + 1 < valid;
-                    const float g0 = v0 ? gn0 : 0.f, g1 = v1 ? gn1 : 0.f, b0 = v0 ? bn0 : 0.f, b1 = v1 ? bn1 : 0.f;
-                    if (n + NP < NC) load_gates(n + NP);
-                    float s = g0 + g1;
-#pragma unroll
-                    for (int off = 1; off < 32; off <<= 1) {
-                        const float t = __shfl_up_sync(0xffffffffu, s, off);
-                        if (lane >= off) s += t;
-                    }
-                    const float c1 = s, c0 = s - g1;
-                    const float cL = __shfl_sync(0xffffffffu, c1, 31);
-                    c_s[2 * lane] = c0;
-                    c_s[2 * lane + 1] = c1;
-                    beta_s[2 * lane] = b0;
-                    beta_s[2 * lane + 1] = b1;
-                    ec_s[2 * lane] = ex2f(c0 * LOG2E);
-                    ec_s[2 * lane + 1] = ex2f(c1 * LOG2E);
-                    ed_s[2 * lane] = ex2f((cL - c0) * LOG2E);
-                    ed_s[2 * lane + 1] = ex2f((cL - c1) * LOG2E);
-                }
-                csync();  // warps 1-7 wait here rather than polling the q / k barriers meanwhile
+                wait_bar(B_GREADY + (k & 1), (uint32_t)((k >> 1) & 1));
                 wait_bar(B_Q, ph);
                 wait_bar(B_K, ph);
                 if (tid == 0) {
@@ -449,39 +421,39 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 csync();
                 wait_mma();
                 if (tid == 0 && n + NP < NC) load_q(n + NP);  // P1 has read q
-                {   // rows 0-63: M (hi/lo -> staging); rows 64-127: L
+                {   // rows 0-63: M = scale (q_i k_j) e^{c_i - c_j}, j <= i (hi/lo -> staging);
+                    // rows 64-127: L = beta_i (k_i k_j) e^{c_i - c_j}, j < i (fp32 scratch).
+                    // One loop for both, so that the loop body's code stays small.
                     float v[32];
                     ptx::tmem_ld32(tl + T_P + 32 * half, v);
                     ptx::tmem_wait_ld();
-                    if (row < CS) {
-                        const int i = row;
-                        const float ci = c_s[i];
-                        float m[32];
+                    const bool mrow = row < CS;
+                    const int i = mrow ? row : row - CS;
+                    const float ci = c_s[i];
+                    const float mul = mrow ? p.scale : beta_s[i];
+                    const int jmax = mrow ? i : i - 1;  // last column kept
 #pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) {
-                            const int j = 32 * half + jj;
-                            m[jj] = (j <= i) ? v[jj] * p.scale * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 c4 = ld4(c_s + 32 * half + 4 * j4);
+                        const float cj[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int jj = 4 * j4 + u, j = 32 * half + jj;
+                            v[jj] = (j <= jmax) ? mul * v[jj] * ex2f((ci - cj[u]) * LOG2E) : 0.f;
                         }
+                    }
+                    if (mrow) {
 #pragma unroll
                         for (int ch = 0; ch < 4; ++ch) {
                             const uint32_t co = sw_chunk(i, 4 * half + ch, 64);
-                            put8_split(sb + stg + SL_M + co, sb + stg + SL_M + 8192 + co, m + 8 * ch, true);
+                            put8_split(sb + stg + SL_M + co, sb + stg + SL_M + 8192 + co, v + 8 * ch, true);
                         }
                     } else {
-                        const int i = row - CS;
-                        const float ci = c_s[i], bi = beta_s[i];
                         float* lrow = Ls + i * LSTRIDE + 32 * half;
 #pragma unroll
-                        for (int j4 = 0; j4 < 8; ++j4) {
-                            float4 o4;
-                            float* o = reinterpret_cast<float*>(&o4);
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int jj = 4 * j4 + u, j = 32 * half + jj;
-                                o[u] = (j < i) ? bi * v[jj] * ex2f((ci - c_s[j]) * LOG2E) : 0.f;
-                            }
-                            *reinterpret_cast<float4*>(lrow + 4 * j4) = o4;
-                        }
+                        for (int j4 = 0; j4 < 8; ++j4)
+                            *reinterpret_cast<float4*>(lrow + 4 * j4) =
+                                make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
                     }
                 }
                 ptx::tc_fence_before();
@@ -507,9 +479,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         put8_split(sb + stg + SL_TP + co, sb + stg + SL_TP + 8192 + co, tp + 8 * hh, true);
                         put8_split(sb + P_TPP + co, sb + P_TPP + 8192 + co, tpp + 8 * hh, true);
                     }
+                    if (tid < 2 * CS)  // decay factors travel with part A of the slot
+                        reinterpret_cast<float*>(smem + stg + SL_EC)[tid] = ec_s[tid];
                 }
                 ptx::fence_proxy_async_smem();
                 csync();
+                if (tid == 0) ptx::mbar_arrive(bar(B_GFREE + (k & 1)));  // gate slot read
                 if (tid == 0) {  // P3: W^T = K^T [T''_hi; T''_lo]^T
                     ptx::tc_fence_after();
 #pragma unroll
@@ -570,6 +545,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // ---------------- output CTA: gated-RMSNorm epilogue of every chunk (4 threads per
             // token, 16-byte chunks {eq, eq+4, eq+8, eq+12}); o arrives from the chain CTA
             const int et = tid >> 2, eq = tid & 3;
+            if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;  // read after the first o slot lands
             auto load_zt = [&](int n) { load_tile(B_ZT + (n & 1), U_Z + (uint32_t)(n & 1) * O_BYTES, &p.tm_z, h, n); };
             if (tid == 0 && p.gated)
                 for (int s = 0; s < 2 && s < NC; ++s) load_zt(s);
@@ -689,6 +665,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         ptx::setmaxnreg_dec<ISSUE_REGS>();
         const bool mma_warp = chain && warp == ISSUER_WARP;
         const bool producer = chain && warp == ISSUER_WARP + 1;
+        const bool mma_out = chain && warp == ISSUER_WARP + 2;
+        const bool gate_warp = !chain && !outcta && warp == ISSUER_WARP;
         auto prep_bar = [&](int b, int m) {  // the prep CTAs' barriers sit at their own misc offset
             return ptx::mapa(sb + P_MISC + M_BAR + 8u * (uint32_t)b, (uint32_t)(1 + m % NSLOT));
         };
@@ -745,22 +723,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         }
                     }
                     commit();
-                    // ---- o1^T = S^T q^T, once the previous chunk's output accumulators are read
-                    wait_bar(B_Q, ph);
-                    if (n > 0) wait_bar(B_OFREE, (uint32_t)((n - 1) & 1));
-                    ptx::tc_fence_after();
-#pragma unroll
-                    for (int part = 0; part < 2; ++part) {
-                        const uint32_t sa = part ? T_SA_LO : T_SA_HI;
-#pragma unroll
-                        for (int s = 0; s < 8; ++s) {
-                            const uint64_t b = ptx::sw128_desc(sb + C_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
-                            ptx::mma_bf16_ts(tmem + T_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
-                        }
-                    }
-                    // ---- dS^T = (v_new e^{cL-c})^T K, o2^T = v_new^T M^T, once v_new is in TMEM
+                    // ---- dS^T = (v_new e^{cL-c})^T K, once v_new is in TMEM
                     wait_bar(B_K, ph);
-                    wait_full(B_FULLB, n);
                     wait_bar(B_VNR, ph);
                     ptx::tc_fence_after();
 #pragma unroll
@@ -773,6 +737,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         }
                     }
                     commit_to(B_X1);
+                }
+                if (*abort_flag) {  // wait (bounded) for every MMA this thread issued
+                    commit_to(B_DRAIN);
+                    ptx::mbar_wait(bar(B_DRAIN), 0u, WAIT_ITERS);
+                }
+            }
+            __syncwarp();
+        } else if (mma_out) {
+            // ---------------- MMA issue for the output terms, off the state recurrence: S^T q^T
+            // while warps 0-7 form v_new (after C12), v_new^T M^T while they update the state
+            // (after dS), so that their issue time does not delay C12 and dS on warp 8.
+            if (lane == 0) {
+                for (int n = 0; n < NC; ++n) {
+                    if (*abort_flag) break;
+                    const uint32_t ph = (uint32_t)(n & 1);
+                    // ---- o1^T = S^T q^T, once the previous chunk's output accumulators are read
+                    wait_bar(B_MMA, ph);  // C12 done: the tensor core is free while v_new is formed
+                    wait_bar(B_Q, ph);
+                    if (n > 0) wait_bar(B_OFREE, (uint32_t)((n - 1) & 1));
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int part = 0; part < 2; ++part) {
+                        const uint32_t sa = part ? T_SA_LO : T_SA_HI;
+#pragma unroll
+                        for (int s = 0; s < 8; ++s) {
+                            const uint64_t b = ptx::sw128_desc(sb + C_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
+                            ptx::mma_bf16_ts(tmem + T_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
+                        }
+                    }
+                    commit_to(B_X2);
+                    // ---- o2^T = v_new^T M^T, once dS is done
+                    wait_bar(B_X1, ph);
+                    wait_bar(B_VNR, ph);
+                    if (ptx::mbar_wait(bar(B_FULLB + n % NSLOT), slot_par(n), WAIT_ITERS)) ++consumed[B_FULLB + n % NSLOT];
+                    else fail();
+                    ptx::tc_fence_after();
                     const uint32_t bp = bslot(n);
 #pragma unroll
                     for (int term = 0; term < 3; ++term) {
@@ -787,8 +787,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     commit_to(B_Y);
                 }
                 if (*abort_flag) {  // wait (bounded) for every MMA this thread issued
-                    commit_to(B_DRAIN);
-                    ptx::mbar_wait(bar(B_DRAIN), 0u, WAIT_ITERS);
+                    commit_to(B_DRAIN2);
+                    ptx::mbar_wait(bar(B_DRAIN2), 0u, WAIT_ITERS);
                 }
             }
             __syncwarp();
@@ -807,7 +807,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     wait_bar(B_VNR, ph);  // C12 read part A; decay factors copied
                     if (n + NSLOT < NC) arm_slot(B_FULLA, n, A_BYTES);
                     ptx::mbar_arrive_remote(prep_bar(B_EMPTYA, n));
-                    wait_bar(B_X1, ph);  // S^T q^T and dS done: q and k tiles free
+                    wait_bar(B_X1, ph);  // dS done: k tile free
+                    wait_bar(B_X2, ph);  // S^T q^T done: q tile free
                     if (n + 1 < NC) {
                         load_q(n + 1);
                         load_k(n + 1);
@@ -826,6 +827,46 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     for (int i = B_FULLA; i < NBAR; ++i)
                         if (issued[i] > 0) ptx::mbar_wait(bar(i), (issued[i] - 1) & 1u, WAIT_ITERS);
                 }
+            }
+            __syncwarp();
+        } else if (gate_warp) {
+            // ---------------- prep CTA: in-chunk cumulative log-decay c (warp scan, lane l holds
+            // tokens 2l and 2l+1), beta, e^c and e^{cL-c} of this CTA's chunks, up to two chunks
+            // ahead of warps 0-7, so that none of it (global loads included) is on their path.
+            const int pi = (int)rank - 1;
+            int k = 0;
+            for (int n = pi; n < NC; n += NP, ++k) {
+                if (*abort_flag) break;
+                if (k >= 2) wait_bar(B_GFREE + (k & 1), (uint32_t)(((k >> 1) - 1) & 1));
+                const int valid = min(CS, len - n * CS);
+                const long long t0 = tok_base + (long long)n * CS;
+                float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
+                if (2 * lane < valid) {
+                    g0 = __ldg(p.g + (size_t)(t0 + 2 * lane) * p.HV + h);
+                    b0 = __ldg(p.beta + (size_t)(t0 + 2 * lane) * p.HV + h);
+                }
+                if (2 * lane + 1 < valid) {
+                    g1 = __ldg(p.g + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
+                    b1 = __ldg(p.beta + (size_t)(t0 + 2 * lane + 1) * p.HV + h);
+                }
+                float sc = g0 + g1;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float t = __shfl_up_sync(0xffffffffu, sc, off);
+                    if (lane >= off) sc += t;
+                }
+                const float c1 = sc, c0 = sc - g1;
+                const float cL = __shfl_sync(0xffffffffu, c1, 31);
+                float* gs = reinterpret_cast<float*>(smem + P_GATE + (uint32_t)(k & 1) * GSLOT);
+                gs[2 * lane] = c0;
+                gs[2 * lane + 1] = c1;
+                gs[CS + 2 * lane] = b0;
+                gs[CS + 2 * lane + 1] = b1;
+                gs[2 * CS + 2 * lane] = ex2f(c0 * LOG2E);
+                gs[2 * CS + 2 * lane + 1] = ex2f(c1 * LOG2E);
+                gs[3 * CS + 2 * lane] = ex2f((cL - c0) * LOG2E);
+                gs[3 * CS + 2 * lane + 1] = ex2f((cL - c1) * LOG2E);
+                ptx::mbar_arrive(bar(B_GREADY + (k & 1)));  // every lane: its stores are released
             }
             __syncwarp();
         } else {
