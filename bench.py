@@ -13,8 +13,9 @@ batch, no collective on the data path; weak scaling), timed on the device with
 CUDA events between barriers, max over ranks.
 
 Prints ONE JSON line (rank 0): the metric of BASELINE.json, whole-job tokens/s,
-plus ``roofline`` (the fused kernel's algorithmic bytes / its CUDA-event
-duration against the measured HBM copy bandwidth), ``cpu_baseline`` (the
+plus ``roofline`` (the prefill kernel's algorithmic bytes / its CUDA-event
+duration against the measured HBM copy bandwidth; config 1 runs the
+cluster-split kernel, config 4 the one-CTA-per-head kernel), ``cpu_baseline`` (the
 reference's own CPU implementation on this host's cores), ``e2e`` (the same
 metric through the public API with pinned host buffers and host<->device
 copies inside the timed region), ``clocks`` (NVML samples taken during the
@@ -80,13 +81,14 @@ def load_peaks():
 
 
 def load_traffic(config):
-    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary, or None."""
+    """(per-launch DRAM bytes, kernel name) of the config's prefill kernel from the committed
+    ncu summary, or (None, None)."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
-        return None
+        return None, None
     d = json.loads(p.read_text())
     v = d.get(f"config{config}")
-    return None if v is None else float(v["dram_bytes_per_launch"])
+    return (None, None) if v is None else (float(v["dram_bytes_per_launch"]), v.get("kernel"))
 
 
 # ----------------------------------------------------------------- clocks
@@ -298,7 +300,7 @@ def main():
     hbm_gbs, tf_burst, tf_sust, peak_kind = load_peaks()
     achieved_gbs = step_bytes / (ms_step / 1e3) / 1e9
     flops = alg_flops(B, T, HV)
-    traffic = load_traffic(args.config)
+    traffic, traffic_kernel = load_traffic(args.config)
     roofline = {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
                 "frac": round(achieved_gbs / hbm_gbs, 4), "traffic": traffic,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
@@ -306,7 +308,8 @@ def main():
                 "tflops_achieved": round(flops / (ms_step / 1e3) / 1e12, 1),
                 "roofline_time_us": round(max(step_bytes / (hbm_gbs * 1e9), flops / (tf_burst * 1e12)) * 1e6, 2),
                 "frac_of_roofline_time": round(max(step_bytes / (hbm_gbs * 1e9), flops / (tf_burst * 1e12))
-                                               / (ms_step / 1e3), 4)}
+                                               / (ms_step / 1e3), 4),
+                "kernel": traffic_kernel}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
