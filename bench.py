@@ -240,6 +240,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     # inputs: rotate through enough copies that each step's working set was evicted from L2
