@@ -825,12 +825,16 @@ cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream)
 int split_cluster_ctas();
 bool split_available();
 
-// Kernel choice: the cluster-split kernel when every (sequence, head) cluster
-// fits on the GPU at once (small batches are latency-bound on the state
-// chain), else the one-CTA-per-head kernel. GDN_B200_KERNEL=fused|split|auto
-// overrides (debug dumps and the pre-stage mode use the one-CTA kernel). A forced
-// split launch fails with cudaErrorNotSupported when the compiled split kernel does
-// not have the register count its register split is written for.
+// Kernel choice: the cluster-split kernel when the (sequence, head) clusters run
+// in at most two waves, else the one-CTA-per-head kernel. Small batches are
+// latency-bound on the state chain: measured on B200, a cluster takes ~3.5 us per
+// chunk and the one-CTA kernel ~11.5 us, so two waves of clusters (B=2, HV=32:
+// 181 vs 233 us at S=1141) still win, three are about even, and with more
+// (sequence, head) units than SMs the one-CTA kernel uses the GPU better.
+// GDN_B200_KERNEL=fused|split|auto overrides (debug dumps and the pre-stage mode
+// use the one-CTA kernel). A forced split launch fails with cudaErrorNotSupported
+// when the compiled split kernel does not have the register count its register
+// split is written for.
 static bool use_split(int nseq, int HV) {
     const char* env = getenv("GDN_B200_KERNEL");
     if (env && strcmp(env, "fused") == 0) return false;
@@ -838,7 +842,8 @@ static bool use_split(int nseq, int HV) {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
-    return (long long)nseq * HV * split_cluster_ctas() <= sms && split_available();
+    const long long per_wave = sms / split_cluster_ctas();
+    return per_wave > 0 && (long long)nseq * HV <= 2 * per_wave && split_available();
 }
 
 struct Launch {
