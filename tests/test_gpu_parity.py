@@ -166,6 +166,18 @@ def test_config1_full_size_gated():
     assert np.array_equal(sf, sf2)
 
 
+def test_config3_long_stream_shard():
+    """BASELINE config 3, one rank's shard: B=1, S=65536, the rank's 4 v-heads (2 qk-heads), zero
+    initial state, fused gated RMSNorm: 1024 chunks of serial state recurrence against the oracle."""
+    inp = make_inputs(1, 65536, 2, 4, 128, seed=3, dist="baseline", with_s0=False)
+    o_ref, sf_ref = O.chunk_gated_delta_rule(inp.q, inp.k, inp.v, inp.g, inp.beta, 64, None)
+    o, sf = run_gpu(inp)
+    check_o(o, o_ref, sf, sf_ref, "config3")
+    y, sf2 = run_gpu(inp, gated=True)
+    check_y(y, O.gated_rmsnorm(o_ref, inp.z, inp.w, inp.eps), "config3-y")
+    assert np.array_equal(sf, sf2)
+
+
 def test_varlen_packed():
     """Config-2-style packed batch (shortened): per-sequence state reset, one state per sequence,
     including an empty and a one-token sequence."""
