@@ -19,7 +19,9 @@ cluster-split kernel, config 4 the one-CTA-per-head kernel), ``cpu_baseline`` (t
 reference's own CPU implementation on this host's cores), ``e2e`` (the same
 metric through the public API with pinned host buffers and host<->device
 copies inside the timed region), ``clocks`` (NVML samples taken during the
-timed region) and ``gpu_launches``.
+timed region), ``gpu_launches`` and ``graph`` (the same launches replayed from
+a CUDA graph of ``--graph-launches`` calls, so that host launch cost is
+visible separately).
 
 ``--impl reference`` times the reference's CPU implementation of the path
 (transformers ``torch_chunk_gated_delta_rule`` + ``Qwen3_5RMSNormGated``, the
@@ -222,6 +224,8 @@ def main():
     ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph-launches", type=int, default=20,
+                    help="launches captured in one CUDA graph for the graph timing (0: skip)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     B, T, HQK, HV = cfg["B"], cfg["T"], cfg["HQK"], cfg["HV"]
@@ -260,13 +264,14 @@ def main():
     import ctypes
     vp = ctypes.c_void_p
 
-    def launch(i):
+    def launch(i, st=None):
         s, (y, sf) = sets[i % n_sets], outs[i % n_sets]
+        st = stream if st is None else st
         rc = lib.deltanet_chunk_prefill_gated(vp(s["q"].data_ptr()), vp(s["k"].data_ptr()), vp(s["v"].data_ptr()),
                                               vp(s["g"].data_ptr()), vp(s["beta"].data_ptr()), vp(s["z"].data_ptr()),
                                               vp(s["w"].data_ptr()), 1e-6, vp(y.data_ptr()),
                                               vp(s["s0"].data_ptr()), vp(sf.data_ptr()), B, T, HV, HQK, D, D, 64,
-                                              vp(ws.data_ptr()), 256, vp(stream.cuda_stream))
+                                              vp(ws.data_ptr()), 256, vp(st.cuda_stream))
         if rc != 0:
             raise RuntimeError(f"deltanet_chunk_prefill_gated returned {rc}")
 
@@ -294,6 +299,35 @@ def main():
     ms_step = ms_total / args.steps
     tokens_step = B * T
     value = world * tokens_step / (ms_step / 1e3)
+
+    # the same launches replayed from a CUDA graph: what is left is GPU-side launch cost
+    graph = None
+    if args.graph_launches > 0:
+        gl = args.graph_launches
+        cap = torch.cuda.Stream(device)
+        cap.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            for i in range(gl):
+                launch(i, cap)
+        g.replay()
+        torch.cuda.synchronize()
+        reps = max(3, min(50, args.steps // gl))
+        ge0, ge1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ge0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        ge1.record(stream)
+        torch.cuda.synchronize()
+        ms_graph = ge0.elapsed_time(ge1)
+        if dist:
+            t = torch.tensor([ms_graph], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_graph = float(t.item())
+        us_call = ms_graph * 1e3 / (reps * gl)
+        graph = {"launches_per_graph": gl, "replays": reps, "us_per_call": round(us_call, 2),
+                 "tokens_per_s": round(world * tokens_step / (us_call / 1e6), 1)}
+        del g
 
     # e2e through the public API: pinned host in, pinned host out, copies inside the timed region
     e2e = run_e2e(args, cfg, device, host_inp, base, world, dist)
@@ -330,7 +364,7 @@ def main():
                        "parallelism": f"batch-sharded x{world}, no collective on the data path",
                        "l2": f"inputs rotate over {n_sets} device copies ({n_sets * step_bytes / 2**20:.0f} MiB > 126 MiB L2)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "clocks": clk.summary(), "gpu_launches": args.steps, "status_word": status,
+            "clocks": clk.summary(), "gpu_launches": args.steps, "status_word": status, "graph": graph,
             "impl": "ours",
         }
         print(json.dumps(line), flush=True)
