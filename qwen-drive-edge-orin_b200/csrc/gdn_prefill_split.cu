@@ -94,8 +94,8 @@ constexpr uint32_t U_OSLOT = 0;                  // 2 o^T slots (chunk parity), 
 constexpr uint32_t U_Z = 2 * O_BYTES;            // 2 z tiles (chunk parity)
 constexpr uint32_t U_OT = U_Z + 2 * O_BYTES;     // o [64 tok][128 dv] (two 64-row panels), transposed here
 constexpr uint32_t U_MISC = U_OT + O_BYTES;
-// ---- misc (all roles; the chain keeps e^c of two chunks in the M_C / M_BETA areas)
-constexpr uint32_t M_C = 0, M_BETA = 256, M_W = 512, M_BAR = 1024, M_TMEM = 1280, M_FLAG = 1284, M_DONE = 1288,
+// ---- misc (all roles; the chain keeps e^c of chunks with even / odd index at M_C, 128 floats)
+constexpr uint32_t M_C = 0, M_W = 512, M_BAR = 1024, M_TMEM = 1280, M_FLAG = 1284, M_DONE = 1288,
                    M_BYTES = 1408;
 constexpr uint32_t MAX2(uint32_t a, uint32_t b) { return a > b ? a : b; }
 constexpr uint32_t SMEM_BYTES = MAX2(MAX2(C_MISC, P_MISC), U_MISC) + M_BYTES;
@@ -189,22 +189,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + misc_off + M_TMEM);
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
 
-    uint32_t issued[NBAR] = {}, consumed[NBAR] = {};
+    // Every wait names its phase parity, derived from the chunk index. The only counts kept
+    // are of the TMA tiles and slot fills a thread arms (scalars, for the abort-path drain):
+    // counters in an array indexed by slot parity would live in local memory, and with most
+    // of the SM's L1 given to shared memory each update is a round trip to L2.
     auto fail = [&]() {
         *abort_flag = 1;
         if (p.status) atomicOr(p.status, 1u);
     };
     auto wait_bar = [&](int i, uint32_t parity) {
-        if (ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) ++consumed[i];
-        else fail();
+        if (!ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) fail();
     };
-    auto wait_mma = [&]() {
-        wait_bar(B_MMA, consumed[B_MMA] & 1u);
+    auto wait_mma = [&](uint32_t parity) {
+        wait_bar(B_MMA, parity);
         ptx::tc_fence_after();
     };
-    auto commit_to = [&](int b) {
+    auto commit_to = [&](int b) { ptx::mma_commit(bar(b)); };
+    // abort path: wait (bounded) for the last phase armed on a barrier (re-armed only after
+    // its previous phase was consumed), and for every MMA this thread issued
+    auto drain = [&](int b, uint32_t armed) {
+        if (armed > 0) ptx::mbar_wait(bar(b), (armed - 1) & 1u, WAIT_ITERS);
+    };
+    auto drain_mma = [&](int b) {
         ptx::mma_commit(bar(b));
-        ++issued[b];
+        ptx::mbar_wait(bar(b), 0u, WAIT_ITERS);
     };
     auto commit = [&]() { commit_to(B_MMA); };
     auto csync = [] { ptx::named_sync(CSYNC, NCOMPUTE); };
@@ -215,8 +223,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(b));
     };
-    auto load_tile = [&](int b, uint32_t dst, const CUtensorMap* map, int head, int n) {
-        ++issued[b];
+    auto load_tile = [&](int b, uint32_t dst, const CUtensorMap* map, int head, int n, uint32_t& armed) {
+        ++armed;
         ptx::mbar_arrive_expect_tx(bar(b), 16384);
         const int t = t_begin + n * CS;
         ptx::tma_load_4d(sb + dst, map, bar(b), 0, head, t, bcoord);
@@ -224,9 +232,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                          bcoord);
     };
     // q -> rows 0-63 and k -> rows 64-127 of the 128-row qk panels; v, z -> 64-row panels
-    auto load_q = [&](int n) { load_tile(B_Q, C_QK, &p.tm_q, hq, n); };
-    auto load_k = [&](int n) { load_tile(B_K, C_QK + 8192, &p.tm_k, hq, n); };
-    auto load_v = [&](int n) { load_tile(B_V, C_V, &p.tm_v, h, n); };
+    // phases armed by this thread: q, k, v tiles; z tiles, slot parts A and B, o slots by parity
+    uint32_t armed_q = 0, armed_k = 0, armed_v = 0, armed_z0 = 0, armed_z1 = 0;
+    uint32_t armed_a0 = 0, armed_a1 = 0, armed_b0 = 0, armed_b1 = 0, armed_o0 = 0, armed_o1 = 0;
+    auto load_q = [&](int n) { load_tile(B_Q, C_QK, &p.tm_q, hq, n, armed_q); };
+    auto load_k = [&](int n) { load_tile(B_K, C_QK + 8192, &p.tm_k, hq, n, armed_k); };
+    auto load_v = [&](int n) { load_tile(B_V, C_V, &p.tm_v, h, n, armed_v); };
     // L2 prefetch of a later chunk's tile (both 64-column boxes), so that its TMA load is an L2 hit
     auto prefetch_tile = [&](const CUtensorMap* map, int head, int n) {
         if (n * CS >= len) return;
@@ -261,7 +272,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         };
         if (outcta && tid == 0) {  // arm the o slots for the first two chunks
             for (int s = 0; s < 2 && s < NC; ++s) {
-                ++issued[B_FULLO + s];
+                ++(s ? armed_o1 : armed_o0);
                 ptx::mbar_arrive_expect_tx(bar(B_FULLO + s), O_BYTES);
             }
         }
@@ -282,14 +293,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 ptx::tmem_wait_st();
                 hand_off(B_SOP);
             }
-            float* ecl = misc + M_C / 4;  // e^c of chunks with even / odd index (M_C, M_BETA areas)
+            float* ecl = misc + M_C / 4;  // e^c of chunks with even / odd index
             for (int n = 0; n < NC; ++n) {
                 if (vote_abort()) break;
                 const uint32_t ph = (uint32_t)(n & 1);
                 const float* ecn = ecl + (n & 1) * CS;
 
                 // ---- v_new hi/lo and (v_new e^{cL-c}) hi/lo -> TMEM A operands; keep e^c
-                wait_mma();
+                wait_mma(ph);
                 if (!ptx::mbar_wait(bar(B_FULLA + n % NSLOT), slot_par(n), WAIT_ITERS)) fail();  // decay factors landed
                 {
                     const uint32_t sp = aslot(n);
@@ -419,7 +430,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     commit();
                 }
                 csync();
-                wait_mma();
+                wait_mma(0u);  // P1: the CTA's commits alternate P1 (even phases) and P3 (odd)
                 if (tid == 0 && n + NP < NC) load_q(n + NP);  // P1 has read q
                 {   // rows 0-63: M = scale (q_i k_j) e^{c_i - c_j}, j <= i (hi/lo -> staging);
                     // rows 64-127: L = beta_i (k_i k_j) e^{c_i - c_j}, j < i (fp32 scratch).
@@ -495,7 +506,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     }
                     commit();
                 }
-                wait_mma();
+                wait_mma(1u);  // P3
                 if (tid == 0 && n + NP < NC) {  // k consumed: fetch this CTA's next chunk
                     load_k(n + NP);
                     prefetch_tile(&p.tm_q, hq, n + 2 * NP);
@@ -519,8 +530,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 csync();
                 if (tid == 0) {  // ship each part once the chain has handed back that part of the previous chunk
                     auto wait_empty = [&](int b) {
-                        if (ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) ++consumed[b];
-                        else fail();
+                        if (!ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) fail();
                     };
                     // the chain CTA's slots and barriers sit at its own offsets
                     const uint32_t fa = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLA + pi), 0);
@@ -537,8 +547,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             if (tid == 0 && k >= 1 && !*abort_flag) {  // the last shipment must land before this CTA exits
 #pragma unroll
                 for (int b = B_EMPTYA; b <= B_EMPTYB; ++b) {
-                    if (ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) ++consumed[b];
-                    else fail();
+                    if (!ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) fail();
                 }
             }
         } else {
@@ -546,7 +555,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // token, 16-byte chunks {eq, eq+4, eq+8, eq+12}); o arrives from the chain CTA
             const int et = tid >> 2, eq = tid & 3;
             if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;  // read after the first o slot lands
-            auto load_zt = [&](int n) { load_tile(B_ZT + (n & 1), U_Z + (uint32_t)(n & 1) * O_BYTES, &p.tm_z, h, n); };
+            auto load_zt = [&](int n) {
+                if (n & 1) load_tile(B_ZT + 1, U_Z + O_BYTES, &p.tm_z, h, n, armed_z1);
+                else load_tile(B_ZT, U_Z, &p.tm_z, h, n, armed_z0);
+            };
             if (tid == 0 && p.gated)
                 for (int s = 0; s < 2 && s < NC; ++s) load_zt(s);
             for (int n = 0; n < NC; ++n) {
@@ -576,7 +588,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 csync();  // o slot read, o staged
                 if (tid == 0) {
                     if (n + 2 < NC) {  // this parity's slot takes chunk n + 2
-                        ++issued[B_FULLO + (n & 1)];
+                        if (n & 1) ++armed_o1;
+                        else ++armed_o0;
                         ptx::mbar_arrive_expect_tx(bar(B_FULLO + (n & 1)), O_BYTES);
                     }
                     // the chain CTA's barriers sit at its own misc offset
@@ -637,26 +650,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 }
             }
             // Abort path: wait (bounded) for the z loads and the chain's o copies armed here
-            if (*abort_flag && tid == 0)
-                for (int i = B_FULLO; i < B_ZT + 2; ++i)
-                    while (consumed[i] < issued[i]) {
-                        ptx::mbar_wait(bar(i), consumed[i] & 1u, WAIT_ITERS);
-                        ++consumed[i];
-                    }
+            if (*abort_flag && tid == 0) {
+                drain(B_FULLO, armed_o0);
+                drain(B_FULLO + 1, armed_o1);
+                drain(B_ZT, armed_z0);
+                drain(B_ZT + 1, armed_z1);
+            }
         }
         // Abort path: wait (bounded) for the TMA loads and MMAs this thread issued before
         // the shared memory and TMEM are released.
-        if (*abort_flag && tid == 0 && !outcta) {
-            for (int i = B_Q; i <= B_K; ++i)
-                while (consumed[i] < issued[i]) {
-                    ptx::mbar_wait(bar(i), consumed[i] & 1u, WAIT_ITERS);
-                    ++consumed[i];
-                }
-            if (!chain)
-                while (consumed[B_MMA] < issued[B_MMA]) {
-                    ptx::mbar_wait(bar(B_MMA), consumed[B_MMA] & 1u, WAIT_ITERS);
-                    ++consumed[B_MMA];
-                }
+        if (*abort_flag && tid == 0 && !chain && !outcta) {  // prep: q / k tiles, P1 / P3
+            drain(B_Q, armed_q);
+            drain(B_K, armed_k);
+            drain_mma(B_DRAIN);
         }
         csync();
         if (tid == 0) *done_flag = 1;  // lets the idle warps of warpgroup 2 stop sleeping
@@ -671,7 +677,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             return ptx::mapa(sb + P_MISC + M_BAR + 8u * (uint32_t)b, (uint32_t)(1 + m % NSLOT));
         };
         auto arm_slot = [&](int b, int m, uint32_t bytes) {
-            ++issued[b + m % NSLOT];
+            const bool odd = (m % NSLOT) != 0;
+            if (b == B_FULLA) ++(odd ? armed_a1 : armed_a0);
+            else ++(odd ? armed_b1 : armed_b0);
             ptx::mbar_arrive_expect_tx(bar(b + m % NSLOT), bytes);
         };
         if (producer && lane == 0) {  // arm the slots for each prep CTA's first chunk
@@ -690,8 +698,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // instruction's execution time, so this warp issues MMAs and waits only on what
             // gates them; loads and slot hand-backs run on the producer warp.
             auto wait_full = [&](int b, int m) {
-                if (ptx::mbar_wait(bar(b + m % NSLOT), slot_par(m), WAIT_ITERS)) ++consumed[b + m % NSLOT];
-                else fail();
+                if (!ptx::mbar_wait(bar(b + m % NSLOT), slot_par(m), WAIT_ITERS)) fail();
             };
             if (lane == 0) {
                 for (int n = 0; n < NC; ++n) {
@@ -738,10 +745,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     }
                     commit_to(B_X1);
                 }
-                if (*abort_flag) {  // wait (bounded) for every MMA this thread issued
-                    commit_to(B_DRAIN);
-                    ptx::mbar_wait(bar(B_DRAIN), 0u, WAIT_ITERS);
-                }
+                if (*abort_flag) drain_mma(B_DRAIN);  // every MMA this thread issued
             }
             __syncwarp();
         } else if (mma_out) {
@@ -770,8 +774,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     // ---- o2^T = v_new^T M^T, once dS is done
                     wait_bar(B_X1, ph);
                     wait_bar(B_VNR, ph);
-                    if (ptx::mbar_wait(bar(B_FULLB + n % NSLOT), slot_par(n), WAIT_ITERS)) ++consumed[B_FULLB + n % NSLOT];
-                    else fail();
+                    if (!ptx::mbar_wait(bar(B_FULLB + n % NSLOT), slot_par(n), WAIT_ITERS)) fail();
                     ptx::tc_fence_after();
                     const uint32_t bp = bslot(n);
 #pragma unroll
@@ -786,10 +789,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     }
                     commit_to(B_Y);
                 }
-                if (*abort_flag) {  // wait (bounded) for every MMA this thread issued
-                    commit_to(B_DRAIN2);
-                    ptx::mbar_wait(bar(B_DRAIN2), 0u, WAIT_ITERS);
-                }
+                if (*abort_flag) drain_mma(B_DRAIN2);  // every MMA this thread issued
             }
             __syncwarp();
         } else if (producer) {
@@ -819,13 +819,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     if (n + NSLOT < NC) arm_slot(B_FULLB, n, B_BYTES);
                     ptx::mbar_arrive_remote(prep_bar(B_EMPTYB, n));
                 }
-                if (*abort_flag) {
-                    // wait (bounded) for the last phase armed on each TMA tile and slot barrier:
-                    // a barrier is re-armed only after its previous phase was consumed
-                    for (int i = B_Q; i <= B_V; ++i)
-                        if (issued[i] > 0) ptx::mbar_wait(bar(i), (issued[i] - 1) & 1u, WAIT_ITERS);
-                    for (int i = B_FULLA; i < NBAR; ++i)
-                        if (issued[i] > 0) ptx::mbar_wait(bar(i), (issued[i] - 1) & 1u, WAIT_ITERS);
+                if (*abort_flag) {  // the TMA tiles and slot fills this thread armed
+                    drain(B_Q, armed_q);
+                    drain(B_K, armed_k);
+                    drain(B_V, armed_v);
+                    drain(B_FULLA, armed_a0);
+                    drain(B_FULLA + 1, armed_a1);
+                    drain(B_FULLB, armed_b0);
+                    drain(B_FULLB + 1, armed_b1);
                 }
             }
             __syncwarp();
