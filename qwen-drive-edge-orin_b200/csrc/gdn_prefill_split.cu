@@ -116,19 +116,22 @@ enum {
     B_FULLA = 11 /* chain: NSLOT */, B_FULLB = B_FULLA + NSLOT /* chain: NSLOT */,
     B_EMPTYO = B_FULLB + NSLOT /* chain: 2 */,
     B_X2 = B_EMPTYO + 2 /* chain: S^T q^T done */, B_DRAIN2 = B_X2 + 1 /* chain: output-MMA warp, abort path */,
+    B_TSFREE = B_DRAIN2 + 1 /* chain: dS read by the state update (one arrival per thread) */,
     B_EMPTYA = 11 /* prep */, B_EMPTYB = 12 /* prep */,
     B_GREADY = 13 /* prep: 2, gate slot written (32 arrivals) */, B_GFREE = 15 /* prep: 2, gate slot read */,
     B_FULLO = 11 /* output: 2 */, B_ZT = 13 /* output: 2 */
 };
-constexpr int NBAR = B_DRAIN2 + 1;
+constexpr int NBAR = B_TSFREE + 1;
 static_assert(B_GFREE + 2 <= NBAR, "prep barriers exceed the barrier area");
 static_assert(M_BAR + 8 * NBAR <= M_TMEM, "barriers overlap the TMEM address word");
 
 // ---- TMEM
-// chain: [0,128) C12 [hi | lo] -> v_new^T hi/lo [0,64) + (v_new e^{cL-c})^T hi/lo [64,128);
-//        [128,192) S^T q^T; [192,256) v_new^T M^T; [256,384) dS^T; [384,512) S^T hi/lo (A operand)
-constexpr uint32_t T_V = 0, T_VN_HI = 0, T_VN_LO = 32, T_VP_HI = 64, T_VP_LO = 96, T_O = 128, T_O2 = 192,
-                   T_S = 256, T_SA_HI = 384, T_SA_LO = 448;
+// chain: [0,128) v_new^T hi/lo [0,64) + (v_new e^{cL-c})^T hi/lo [64,128) (A operands);
+//        [128,192) S^T q^T; [192,256) v_new^T M^T; [256,384) C12 [hi | lo], then dS^T; [384,512)
+//        S^T hi/lo (A operand). C12 of chunk n+1 may start once the state update has read dS of
+//        chunk n, and the v_new operands are not written over their own input.
+constexpr uint32_t T_VN_HI = 0, T_VN_LO = 32, T_VP_HI = 64, T_VP_LO = 96, T_O = 128, T_O2 = 192,
+                   T_S = 256, T_C12 = T_S, T_SA_HI = 384, T_SA_LO = 448;
 // prep: [0,64) P1; [128,256) P3 [T''_hi | T''_lo] parts of W^T
 constexpr uint32_t T_P = 0, T_W = 128;
 
@@ -172,7 +175,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
     if (tid == 0) {
         for (int i = 0; i < NBAR; ++i)
-            ptx::mbar_init(bar(i), (chain && i >= B_VNR && i <= B_OFREE)                      ? (uint32_t)NCOMPUTE
+            ptx::mbar_init(bar(i), (chain && ((i >= B_VNR && i <= B_OFREE) || i == B_TSFREE)) ? (uint32_t)NCOMPUTE
                                    : (!chain && !outcta && (i == B_GREADY || i == B_GREADY + 1)) ? 32u
                                                                                                : 1u);
         ptx::fence_mbar_init();
@@ -308,8 +311,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     float v[32];
                     {
                         float v2[32];
-                        ptx::tmem_ld32(tl + T_V + 32 * half, v);
-                        ptx::tmem_ld32(tl + T_V + 64 + 32 * half, v2);
+                        ptx::tmem_ld32(tl + T_C12 + 32 * half, v);
+                        ptx::tmem_ld32(tl + T_C12 + 64 + 32 * half, v2);
                         ptx::tmem_wait_ld();
 #pragma unroll
                         for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
@@ -325,9 +328,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         split2(v[2 * j + 2] * e4.z, v[2 * j + 3] * e4.w, ph_[j + 1], pl[j + 1]);
                     }
                     if (tid < CS) ecl[(n & 1) * CS + tid] = reinterpret_cast<const float*>(smem + sp + A_EC)[tid];
-                    ptx::tc_fence_before();
-                    csync();  // all of cols [0,128) read before they are overwritten; e^c copied
-                    ptx::tc_fence_after();
+                    // the previous chunk's v_new^T M^T and dS have read these columns (Y and X1 waited)
                     ptx::tmem_st16(tl + T_VN_HI + 16 * half, vh);
                     ptx::tmem_st16(tl + T_VN_LO + 16 * half, vl);
                     ptx::tmem_st16(tl + T_VP_HI + 16 * half, ph_);
@@ -335,6 +336,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ptx::tmem_wait_st();
                     hand_off(B_VNR);
                 }
+                csync();  // e^c copied for every thread
 
                 // ---- S <- e^{cL} S + dS; the new S^T hi/lo operand (S^T q^T has read the old one)
                 wait_bar(B_X1, ph);
@@ -346,6 +348,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         float v[32];
                         ptx::tmem_ld32(tl + T_S + 64 * half + 32 * c2, v);
                         ptx::tmem_wait_ld();
+                        if (c2 == 1) hand_off(B_TSFREE);  // dS read: C12 of the next chunk may start
 #pragma unroll
                         for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
                     }
@@ -709,13 +712,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     //      the v^T T'^T part does not depend on the state and goes first
                     wait_full(B_FULLA, n);
                     wait_bar(B_V, ph);
-                    if (n > 0) wait_bar(B_Y, (uint32_t)((n - 1) & 1));  // v_new operands of chunk n-1 read
+                    if (n > 0) wait_bar(B_TSFREE, (uint32_t)((n - 1) & 1));  // dS of chunk n-1 read
                     ptx::tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         const uint64_t a = ptx::sw128_desc(sb + C_V + s * 2048, 8192, 1024);
                         const uint64_t b = ptx::sw128_desc(sb + sp + A_TP + s * 32, 16, 1024);
-                        ptx::mma_bf16(tmem + T_V, a, b, ID_U, s > 0);
+                        ptx::mma_bf16(tmem + T_C12, a, b, ID_U, s > 0);
                     }
                     commit_to(B_VT);      // the v tile is free once these have run
                     wait_bar(B_SOP, ph);  // S_n^T hi/lo in TMEM
@@ -726,7 +729,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 #pragma unroll
                         for (int s = 0; s < 8; ++s) {
                             const uint64_t b = ptx::sw128_desc(sb + sp + A_W + s * 2048, 16384, 1024);
-                            ptx::mma_bf16_ts(tmem + T_V, tmem + sa + 8 * s, b, ID_WS, 1u);
+                            ptx::mma_bf16_ts(tmem + T_C12, tmem + sa + 8 * s, b, ID_WS, 1u);
                         }
                     }
                     commit();
