@@ -82,11 +82,10 @@ constexpr uint32_t C_ASLOT = C_OST + 2 * O_BYTES;       // NSLOT part-A slots
 constexpr uint32_t C_BSLOT = C_ASLOT + NSLOT * ASLOT;   // NSLOT part-B slots (M)
 constexpr uint32_t C_MISC = C_BSLOT + NSLOT * B_BYTES;
 // ---- prep CTA shared memory
-constexpr uint32_t P_QK = 0;                     // 2 q|k buffers (chunk parity), 32 KB each
-constexpr uint32_t QKBUF = 32768;
-constexpr uint32_t P_L = 2 * QKBUF;              // L / T fp32 [64][68]
-constexpr uint32_t P_STG = 82944;                // 2 staging slots (1024-aligned); T'' hi/lo sits in a
-                                                 // slot's W area between the T split and P3
+constexpr uint32_t P_QK = 0;
+constexpr uint32_t P_L = 32768;                  // L / T fp32 [64][68]
+constexpr uint32_t P_TPP = 50176;                // T'' hi, lo [64][64] bf16
+constexpr uint32_t P_STG = 66560;                // 2 staging slots
 constexpr uint32_t P_GATE = P_STG + 2 * SLOT;    // 2 gate slots (chunk parity): c, beta, e^c, e^{cL-c} [64] f32
 constexpr uint32_t GSLOT = 1024;
 constexpr uint32_t P_MISC = P_GATE + 2 * GSLOT;
@@ -102,8 +101,7 @@ constexpr uint32_t MAX2(uint32_t a, uint32_t b) { return a > b ? a : b; }
 constexpr uint32_t SMEM_BYTES = MAX2(MAX2(C_MISC, P_MISC), U_MISC) + M_BYTES;
 constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory limit");
-static_assert(P_L + 64 * LSTRIDE * 4 <= P_STG, "L scratch overlaps the staging slots");
-static_assert(P_STG % 1024 == 0, "staging slots hold 128B-swizzled tiles");
+static_assert(P_L + 64 * LSTRIDE * 4 <= P_TPP, "L scratch overlaps T''");
 
 // barrier slots: TMA tiles; MMA commit groups (chain: B_VT = v^T T'^T, the part of C12 that
 // reads the v tile, B_MMA = C12, X1 = S^T q^T + dS, Y = v_new^T M^T; B_DRAIN only on the
@@ -120,8 +118,6 @@ enum {
     B_X2 = B_EMPTYO + 2 /* chain: S^T q^T done */, B_DRAIN2 = B_X2 + 1 /* chain: output-MMA warp, abort path */,
     B_TSFREE = B_DRAIN2 + 1 /* chain: dS read by the state update (one arrival per thread) */,
     B_EMPTYA = 11 /* prep */, B_EMPTYB = 12 /* prep */,
-    B_QB1 = 2 /* prep: q tile, buffer 1 */, B_KB1 = 4 /* prep: k tile, buffer 1 */,
-    B_P1C = 5 /* prep: P1 commits (gate warp) */, B_TPFREE = 7 /* prep: P1 accumulator read */,
     B_GREADY = 13 /* prep: 2, gate slot written (32 arrivals) */, B_GFREE = 15 /* prep: 2, gate slot read */,
     B_FULLO = 11 /* output: 2 */, B_ZT = 13 /* output: 2 */
 };
@@ -230,33 +226,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(b));
     };
-    // one 64-token tile (two 64-column boxes): q / k tiles are the upper / lower 64 rows of two
-    // 128-row panels (second box 16 KB on), v / z tiles two 64-row panels (8 KB on)
-    auto load_tile = [&](int b, uint32_t dst, const CUtensorMap* map, int head, int n, uint32_t& armed,
-                         uint32_t box2) {
+    auto load_tile = [&](int b, uint32_t dst, const CUtensorMap* map, int head, int n, uint32_t& armed) {
         ++armed;
         ptx::mbar_arrive_expect_tx(bar(b), 16384);
         const int t = t_begin + n * CS;
         ptx::tma_load_4d(sb + dst, map, bar(b), 0, head, t, bcoord);
-        ptx::tma_load_4d(sb + dst + box2, map, bar(b), 64, head, t, bcoord);
+        ptx::tma_load_4d(sb + dst + (dst == C_QK || dst == C_QK + 8192 ? 16384 : 8192), map, bar(b), 64, head, t,
+                         bcoord);
     };
     // q -> rows 0-63 and k -> rows 64-127 of the 128-row qk panels; v, z -> 64-row panels
     // phases armed by this thread: q, k, v tiles; z tiles, slot parts A and B, o slots by parity
-    uint32_t armed_q = 0, armed_k = 0, armed_v = 0, armed_z0 = 0, armed_z1 = 0, armed_q1 = 0, armed_k1 = 0;
+    uint32_t armed_q = 0, armed_k = 0, armed_v = 0, armed_z0 = 0, armed_z1 = 0;
     uint32_t armed_a0 = 0, armed_a1 = 0, armed_b0 = 0, armed_b1 = 0, armed_o0 = 0, armed_o1 = 0;
-    auto load_q = [&](int n) { load_tile(B_Q, C_QK, &p.tm_q, hq, n, armed_q, 16384); };
-    auto load_k = [&](int n) { load_tile(B_K, C_QK + 8192, &p.tm_k, hq, n, armed_k, 16384); };
-    auto load_v = [&](int n) { load_tile(B_V, C_V, &p.tm_v, h, n, armed_v, 8192); };
-    // prep: q and k of chunk n into q|k buffer `buf`
-    auto load_qk_buf = [&](int n, int buf) {
-        if (buf) {
-            load_tile(B_QB1, P_QK + QKBUF, &p.tm_q, hq, n, armed_q1, 16384);
-            load_tile(B_KB1, P_QK + QKBUF + 8192, &p.tm_k, hq, n, armed_k1, 16384);
-        } else {
-            load_tile(B_Q, P_QK, &p.tm_q, hq, n, armed_q, 16384);
-            load_tile(B_K, P_QK + 8192, &p.tm_k, hq, n, armed_k, 16384);
-        }
-    };
+    auto load_q = [&](int n) { load_tile(B_Q, C_QK, &p.tm_q, hq, n, armed_q); };
+    auto load_k = [&](int n) { load_tile(B_K, C_QK + 8192, &p.tm_k, hq, n, armed_k); };
+    auto load_v = [&](int n) { load_tile(B_V, C_V, &p.tm_v, h, n, armed_v); };
     // L2 prefetch of a later chunk's tile (both 64-column boxes), so that its TMA load is an L2 hit
     auto prefetch_tile = [&](const CUtensorMap* map, int head, int n) {
         if (n * CS >= len) return;
@@ -417,9 +401,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // ---------------- prep CTA
             const int pi = (int)rank - 1;  // owns chunks pi, pi + NP, ...
             float* Ls = reinterpret_cast<float*>(smem + P_L);
-            if (tid == 0) {  // this CTA's first two chunks into the two q|k buffers
-                if (pi < NC) load_qk_buf(pi, 0);
-                if (pi + NP < NC) load_qk_buf(pi + NP, 1);
+            if (tid == 0 && pi < NC) {
+                load_q(pi);
+                load_k(pi);
             }
 
             int k = 0;
@@ -434,10 +418,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 // thread takes the same exit decision
                 if (vote_abort()) break;
 
-                const uint32_t qkb = P_QK + (uint32_t)(k & 1) * QKBUF;  // this chunk's q|k buffer
                 wait_bar(B_GREADY + (k & 1), (uint32_t)((k >> 1) & 1));
-                wait_bar(B_P1C, ph);  // P1, issued by the gate warp while the previous chunk ran
-                ptx::tc_fence_after();
+                wait_bar(B_Q, ph);
+                wait_bar(B_K, ph);
+                if (tid == 0) {
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int s = 0; s < 8; ++s) {
+                        const uint32_t koff = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
+                        const uint64_t a = ptx::sw128_desc(sb + P_QK + koff, 16, 1024);
+                        const uint64_t b = ptx::sw128_desc(sb + P_QK + 8192 + koff, 16, 1024);
+                        ptx::mma_bf16(tmem + T_P, a, b, ID_P, s > 0);
+                    }
+                    commit();
+                }
+                csync();
+                wait_mma(0u);  // P1: the CTA's commits alternate P1 (even phases) and P3 (odd)
+                if (tid == 0 && n + NP < NC) load_q(n + NP);  // P1 has read q
                 {   // rows 0-63: M = scale (q_i k_j) e^{c_i - c_j}, j <= i (hi/lo -> staging);
                     // rows 64-127: L = beta_i (k_i k_j) e^{c_i - c_j}, j < i (fp32 scratch).
                     // One loop for both, so that the loop body's code stays small.
@@ -475,9 +472,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 }
                 ptx::tc_fence_before();
                 csync();
-                if (tid == 0) ptx::mbar_arrive(bar(B_TPFREE));  // P1 accumulator read: the next P1 may go
                 invert_unit_lower(Ls, X, tid, [](int) {}, csync);
-                {   // T' -> staging (stacked hi/lo); T'' -> the staging slot's W area until P3 has read it
+                {   // T' -> staging (stacked hi/lo), T'' -> local
                     const int i = tid >> 2, jb = tid & 3;
                     float tp[16], tpp[16];
 #pragma unroll
@@ -495,7 +491,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     for (int hh = 0; hh < 2; ++hh) {
                         const uint32_t co = sw_chunk(i, 2 * jb + hh, 64);
                         put8_split(sb + stg + SL_TP + co, sb + stg + SL_TP + 8192 + co, tp + 8 * hh, true);
-                        put8_split(sb + stg + SL_W + co, sb + stg + SL_W + 8192 + co, tpp + 8 * hh, true);
+                        put8_split(sb + P_TPP + co, sb + P_TPP + 8192 + co, tpp + 8 * hh, true);
                     }
                     if (tid < 2 * CS)  // decay factors travel with part A of the slot
                         reinterpret_cast<float*>(smem + stg + SL_EC)[tid] = ec_s[tid];
@@ -504,21 +500,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 csync();
                 if (tid == 0) ptx::mbar_arrive(bar(B_GFREE + (k & 1)));  // gate slot read
                 if (tid == 0) {  // P3: W^T = K^T [T''_hi; T''_lo]^T
-                    wait_bar((k & 1) ? B_KB1 : B_K, (uint32_t)((k >> 1) & 1));  // (observed by this thread too)
                     ptx::tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
-                        const uint64_t a = ptx::sw128_desc(sb + qkb + 8192 + s * 2048, 16384, 1024);
-                        const uint64_t b = ptx::sw128_desc(sb + stg + SL_W + s * 32, 16, 1024);
+                        const uint64_t a = ptx::sw128_desc(sb + P_QK + 8192 + s * 2048, 16384, 1024);
+                        const uint64_t b = ptx::sw128_desc(sb + P_TPP + s * 32, 16, 1024);
                         ptx::mma_bf16(tmem + T_W, a, b, ID_W, s > 0);
                     }
                     commit();
                 }
-                wait_mma(ph);  // P3 (one commit per chunk)
-                if (tid == 0 && n + 2 * NP < NC) {  // P1 and P3 have read this buffer: chunk k + 2 goes in
-                    load_qk_buf(n + 2 * NP, k & 1);
-                    prefetch_tile(&p.tm_q, hq, n + 3 * NP);
-                    prefetch_tile(&p.tm_k, hq, n + 3 * NP);
+                wait_mma(1u);  // P3
+                if (tid == 0 && n + NP < NC) {  // k consumed: fetch this CTA's next chunk
+                    load_k(n + NP);
+                    prefetch_tile(&p.tm_q, hq, n + 2 * NP);
+                    prefetch_tile(&p.tm_k, hq, n + 2 * NP);
                 }
                 {   // W^T rows (dk = row) -> staging, hi and lo tiles 16 KB apart
                     float v[32], v2[32];
@@ -564,8 +559,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             const int et = tid >> 2, eq = tid & 3;
             if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;  // read after the first o slot lands
             auto load_zt = [&](int n) {
-                if (n & 1) load_tile(B_ZT + 1, U_Z + O_BYTES, &p.tm_z, h, n, armed_z1, 8192);
-                else load_tile(B_ZT, U_Z, &p.tm_z, h, n, armed_z0, 8192);
+                if (n & 1) load_tile(B_ZT + 1, U_Z + O_BYTES, &p.tm_z, h, n, armed_z1);
+                else load_tile(B_ZT, U_Z, &p.tm_z, h, n, armed_z0);
             };
             if (tid == 0 && p.gated)
                 for (int s = 0; s < 2 && s < NC; ++s) load_zt(s);
@@ -667,11 +662,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         }
         // Abort path: wait (bounded) for the TMA loads and MMAs this thread issued before
         // the shared memory and TMEM are released.
-        if (*abort_flag && tid == 0 && !chain && !outcta) {  // prep: q / k tiles, P3
+        if (*abort_flag && tid == 0 && !chain && !outcta) {  // prep: q / k tiles, P1 / P3
             drain(B_Q, armed_q);
             drain(B_K, armed_k);
-            drain(B_QB1, armed_q1);
-            drain(B_KB1, armed_k1);
             drain_mma(B_DRAIN);
         }
         csync();
@@ -878,29 +871,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 gs[3 * CS + 2 * lane] = ex2f((cL - c0) * LOG2E);
                 gs[3 * CS + 2 * lane + 1] = ex2f((cL - c1) * LOG2E);
                 ptx::mbar_arrive(bar(B_GREADY + (k & 1)));  // every lane: its stores are released
-                // P1 of this chunk: [Q;K] K^T into the P1 accumulator, once warps 0-7 have read the
-                // previous chunk's and this chunk's q|k buffer has landed; it runs during the
-                // previous chunk's triangular inverse.
-                __syncwarp();
-                if (lane == 0) {
-                    const uint32_t qkb = P_QK + (uint32_t)(k & 1) * QKBUF;
-                    const uint32_t qpar = (uint32_t)((k >> 1) & 1);
-                    if (k >= 1) wait_bar(B_TPFREE, (uint32_t)((k - 1) & 1));
-                    wait_bar((k & 1) ? B_QB1 : B_Q, qpar);
-                    wait_bar((k & 1) ? B_KB1 : B_K, qpar);
-                    ptx::tc_fence_after();
-#pragma unroll
-                    for (int s = 0; s < 8; ++s) {
-                        const uint32_t koff = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
-                        const uint64_t a = ptx::sw128_desc(sb + qkb + koff, 16, 1024);
-                        const uint64_t b = ptx::sw128_desc(sb + qkb + 8192 + koff, 16, 1024);
-                        ptx::mma_bf16(tmem + T_P, a, b, ID_P, s > 0);
-                    }
-                    commit_to(B_P1C);
-                }
-                __syncwarp();
             }
-            if (lane == 0 && *abort_flag) drain_mma(B_DRAIN2);  // every MMA this lane issued
             __syncwarp();
         } else {
             // Idle warps sleep until warps 0-7 are done instead of waiting at the cluster
