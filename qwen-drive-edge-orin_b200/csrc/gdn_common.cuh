@@ -131,8 +131,15 @@ __device__ __forceinline__ void put8_split(uint32_t hi_addr, uint32_t lo_addr, c
 //      lane = column, column in registers);
 //   B/C: 32x32 halves: T_10 = -(T_11 L_10) T_00 and T_32 = -(T_33 L_32) T_22;
 //   D/E: T_[32:,:32] = -(T_[32:,32:] L_[32:,:32]) T_[:32,:32].
-// Every product is register-blocked 1x4 with 16-byte loads and uses the
-// triangular structure to skip zero terms. X holds the left products.
+// The block products B-E are small (16x16x16 and 32x32x32) and sit on a chain of
+// dependent steps. Two implementations, chosen by the template flag:
+//   kTensorProducts = true: warp-level m16n8k8 tf32 tensor-core products with fp32
+//     operands split in two tf32 terms (a = a_hi + a_lo; a b ~ a_hi b_hi + a_hi b_lo +
+//     a_lo b_hi, the "3xTF32" scheme, about fp32 accuracy), one 16x8 output tile per
+//     warp; X holds 1152 floats (rows of 36, conflict-free fragment loads).
+//   kTensorProducts = false: CUDA-core products register-blocked 1x4 with 16-byte
+//     loads; X holds 1536 floats.
+// Both skip the tiles or terms that the triangular factors make zero.
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
     acc.x = fmaf(a, b.x, acc.x);
@@ -141,12 +148,65 @@ __device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
     acc.w = fmaf(a, b.w, acc.w);
 }
 
+namespace tf32x3 {
+__device__ __forceinline__ uint32_t round_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ void split(float x, uint32_t& hi, uint32_t& lo) {
+    hi = round_tf32(x);
+    lo = round_tf32(x - __uint_as_float(hi));
+}
+// d += a b for one m16n8k8 tile (row-major A fragment, column-major B fragment)
+__device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Accumulators of one warp's 16x8 tile: main (hi*hi) and correction terms, two sets
+// alternating by k-step so that consecutive products do not wait on each other.
+struct Tile {
+    float m[2][4], c[2][4];
+    __device__ __forceinline__ Tile() {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) m[i][j] = c[i][j] = 0.f;
+    }
+    // += A (16x8, element (r, k) at A[r * lda + k]) * B (8x8, element (k, n) at B[k * ldb + n])
+    __device__ __forceinline__ void step(int par, const float* A, int lda, const float* B, int ldb, int lane) {
+        const int g = lane >> 2, t = lane & 3;
+        uint32_t ah[4], al[4], bh0, bl0, bh1, bl1;
+        split(A[g * lda + t], ah[0], al[0]);
+        split(A[(g + 8) * lda + t], ah[1], al[1]);
+        split(A[g * lda + t + 4], ah[2], al[2]);
+        split(A[(g + 8) * lda + t + 4], ah[3], al[3]);
+        split(B[t * ldb + g], bh0, bl0);
+        split(B[(t + 4) * ldb + g], bh1, bl1);
+        mma(c[par], al, bh0, bh1);
+        mma(m[par], ah, bh0, bh1);
+        mma(c[par], ah, bl0, bl1);
+    }
+    // C (element (r, n) at C[r * ldc + n]) = s * tile
+    __device__ __forceinline__ void store(float* C, int ldc, float s, int lane) const {
+        const int g = lane >> 2, t = lane & 3;
+        float d[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[j] = s * ((m[0][j] + m[1][j]) + (c[0][j] + c[1][j]));
+        *reinterpret_cast<float2*>(C + g * ldc + 2 * t) = make_float2(d[0], d[1]);
+        *reinterpret_cast<float2*>(C + (g + 8) * ldc + 2 * t) = make_float2(d[2], d[3]);
+    }
+};
+}  // namespace tf32x3
+
 // `idle(phase)` runs on threads 128-255 during phases A, B and C (phase = 0, 1, 2),
 // which use only threads 0-127. `sync()` is the barrier over the 256 threads taking
 // part (a block-wide __syncthreads, or a named barrier when other warps of the
 // block do different work).
-template <typename Idle, typename Sync>
+template <bool kTensorProducts, typename Idle, typename Sync>
 __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, Idle&& idle, Sync&& sync) {
+    constexpr int XS = 36;
     const int warp = tid >> 5, lane = tid & 31;
     if (tid >= 128) idle(0);
     // A: diagonal blocks
@@ -171,77 +231,128 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
         for (int i = 0; i < 16; ++i) Tb[i * LSTRIDE + c] = t[i];
     }
     sync();
-    // B: X[0:256] = T_11 L_10, X[256:512] = T_33 L_32   (16x16 each, stride 16).
-    // Terms above the diagonal of T_rr are stored zeros, so every unit runs the
-    // full 16-term range in groups of four with its loads issued together.
-    if (tid >= 128) idle(1);
-    if (tid < 128) {
-        const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
-        const int r0 = 16 + 32 * blk, c0 = 32 * blk;  // T_rr at (r0, r0), L block at (r0, c0)
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* trow = Ls + (r0 + i) * LSTRIDE + r0;
-#pragma unroll
-        for (int m0 = 0; m0 < 16; m0 += 4) {
-            const float4 t4 = ld4(trow + m0);
-            const float4 b0 = ld4(Ls + (r0 + m0) * LSTRIDE + c0 + j0), b1 = ld4(Ls + (r0 + m0 + 1) * LSTRIDE + c0 + j0);
-            const float4 b2 = ld4(Ls + (r0 + m0 + 2) * LSTRIDE + c0 + j0), b3 = ld4(Ls + (r0 + m0 + 3) * LSTRIDE + c0 + j0);
-            fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
+    if constexpr (kTensorProducts) {
+        // B: X_p = T_rr L_rc, 16x16 (p = 0: r = 16, c = 0; p = 1: r = 48, c = 32); warp = (p, n-tile)
+        if (tid >= 128) idle(1);
+        if (warp < 4) {
+            const int pp = warp >> 1, nt = warp & 1, r0 = 16 + 32 * pp, c0 = 32 * pp;
+            tf32x3::Tile acc;
+    #pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+                acc.step(ks, Ls + r0 * LSTRIDE + r0 + 8 * ks, LSTRIDE, Ls + (r0 + 8 * ks) * LSTRIDE + c0 + 8 * nt, LSTRIDE,
+                         lane);
+            acc.store(X + pp * 16 * XS + 8 * nt, XS, 1.f, lane);
         }
-        *reinterpret_cast<float4*>(X + blk * 256 + i * 16 + j0) =
-            make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
-    }
-    sync();
-    // C: T_10 = -X0 T_00 -> rows 16-31, cols 0-15; T_32 = -X1 T_22 -> rows 48-63, cols 32-47
-    if (tid >= 128) idle(2);
-    if (tid < 128) {
-        const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
-        const int d0 = 32 * blk;  // T_ss at (d0, d0)
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* xrow = X + blk * 256 + i * 16;
-#pragma unroll
-        for (int m0 = 0; m0 < 16; m0 += 4) {
-            const float4 x4 = ld4(xrow + m0);
-            const float4 b0 = ld4(Ls + (d0 + m0) * LSTRIDE + d0 + j0), b1 = ld4(Ls + (d0 + m0 + 1) * LSTRIDE + d0 + j0);
-            const float4 b2 = ld4(Ls + (d0 + m0 + 2) * LSTRIDE + d0 + j0), b3 = ld4(Ls + (d0 + m0 + 3) * LSTRIDE + d0 + j0);
-            fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
+        sync();
+        // C: T_rc = -X_p T_cc (T_cc[k][n] = 0 for k < n: n-tile 1 skips k-step 0)
+        if (tid >= 128) idle(2);
+        if (warp < 4) {
+            const int pp = warp >> 1, nt = warp & 1, r0 = 16 + 32 * pp, c0 = 32 * pp;
+            tf32x3::Tile acc;
+    #pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+                if (ks >= nt)
+                    acc.step(ks, X + pp * 16 * XS + 8 * ks, XS, Ls + (c0 + 8 * ks) * LSTRIDE + c0 + 8 * nt, LSTRIDE, lane);
+            acc.store(Ls + r0 * LSTRIDE + c0 + 8 * nt, LSTRIDE, -1.f, lane);
         }
-        *reinterpret_cast<float4*>(Ls + (d0 + 16 + i) * LSTRIDE + d0 + j0) =
-            make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
-    }
-    sync();
-    // D: X[512:1536] = T_[32:,32:] L_[32:,:32]   (32x32, stride 32)
-    {
-        const int i = tid >> 3, j0 = (tid & 7) * 4;
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* trow = Ls + (32 + i) * LSTRIDE + 32;
-        const int mend = (i + 4) & ~3;  // T_[32:,32:][i][m] = 0 for m > i
-#pragma unroll 2
-        for (int m0 = 0; m0 < mend; m0 += 4) {
-            const float4 t4 = ld4(trow + m0);
-            const float4 b0 = ld4(Ls + (32 + m0) * LSTRIDE + j0), b1 = ld4(Ls + (33 + m0) * LSTRIDE + j0);
-            const float4 b2 = ld4(Ls + (34 + m0) * LSTRIDE + j0), b3 = ld4(Ls + (35 + m0) * LSTRIDE + j0);
-            fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
+        sync();
+        // D: X2 = T_[32:,32:] L_[32:,:32] -> X (B's products are dead); rows 0-15 of T_[32:,32:]
+        // are zero beyond column 15. warp = (m-tile, n-tile)
+        {
+            const int mt = warp >> 2, nt = warp & 3;
+            tf32x3::Tile acc;
+    #pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                if (mt == 1 || ks < 2)
+                    acc.step(ks & 1, Ls + (32 + 16 * mt) * LSTRIDE + 32 + 8 * ks, LSTRIDE,
+                             Ls + (32 + 8 * ks) * LSTRIDE + 8 * nt, LSTRIDE, lane);
+            acc.store(X + 16 * mt * XS + 8 * nt, XS, 1.f, lane);
         }
-        *reinterpret_cast<float4*>(X + 512 + i * 32 + j0) =
-            make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
-    }
-    sync();
-    // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j)
-    {
-        const int i = tid >> 3, j0 = (tid & 7) * 4;
-        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-        const float* xrow = X + 512 + i * 32;
-#pragma unroll 2
-        for (int m0 = j0; m0 < 32; m0 += 4) {
-            const float4 x4 = ld4(xrow + m0);
-            const float4 b0 = ld4(Ls + m0 * LSTRIDE + j0), b1 = ld4(Ls + (m0 + 1) * LSTRIDE + j0);
-            const float4 b2 = ld4(Ls + (m0 + 2) * LSTRIDE + j0), b3 = ld4(Ls + (m0 + 3) * LSTRIDE + j0);
-            fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
+        sync();
+        // E: T_[32:,:32] = -X2 T_[:32,:32] (T_[:32,:32][k][n] = 0 for k < n)
+        {
+            const int mt = warp >> 2, nt = warp & 3;
+            tf32x3::Tile acc;
+    #pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                if (ks >= nt)
+                    acc.step(ks & 1, X + 16 * mt * XS + 8 * ks, XS, Ls + (8 * ks) * LSTRIDE + 8 * nt, LSTRIDE, lane);
+            acc.store(Ls + (32 + 16 * mt) * LSTRIDE + 8 * nt, LSTRIDE, -1.f, lane);
         }
-        *reinterpret_cast<float4*>(Ls + (32 + i) * LSTRIDE + j0) =
-            make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
+        sync();
+    } else {
+        // B: X[0:256] = T_11 L_10, X[256:512] = T_33 L_32   (16x16 each, stride 16).
+        // Terms above the diagonal of T_rr are stored zeros, so every unit runs the
+        // full 16-term range in groups of four with its loads issued together.
+        if (tid >= 128) idle(1);
+        if (tid < 128) {
+            const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
+            const int r0 = 16 + 32 * blk, c0 = 32 * blk;  // T_rr at (r0, r0), L block at (r0, c0)
+            float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+            const float* trow = Ls + (r0 + i) * LSTRIDE + r0;
+    #pragma unroll
+            for (int m0 = 0; m0 < 16; m0 += 4) {
+                const float4 t4 = ld4(trow + m0);
+                const float4 b0 = ld4(Ls + (r0 + m0) * LSTRIDE + c0 + j0), b1 = ld4(Ls + (r0 + m0 + 1) * LSTRIDE + c0 + j0);
+                const float4 b2 = ld4(Ls + (r0 + m0 + 2) * LSTRIDE + c0 + j0), b3 = ld4(Ls + (r0 + m0 + 3) * LSTRIDE + c0 + j0);
+                fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
+            }
+            *reinterpret_cast<float4*>(X + blk * 256 + i * 16 + j0) =
+                make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
+        }
+        sync();
+        // C: T_10 = -X0 T_00 -> rows 16-31, cols 0-15; T_32 = -X1 T_22 -> rows 48-63, cols 32-47
+        if (tid >= 128) idle(2);
+        if (tid < 128) {
+            const int blk = tid >> 6, i = (tid >> 2) & 15, j0 = (tid & 3) * 4;
+            const int d0 = 32 * blk;  // T_ss at (d0, d0)
+            float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+            const float* xrow = X + blk * 256 + i * 16;
+    #pragma unroll
+            for (int m0 = 0; m0 < 16; m0 += 4) {
+                const float4 x4 = ld4(xrow + m0);
+                const float4 b0 = ld4(Ls + (d0 + m0) * LSTRIDE + d0 + j0), b1 = ld4(Ls + (d0 + m0 + 1) * LSTRIDE + d0 + j0);
+                const float4 b2 = ld4(Ls + (d0 + m0 + 2) * LSTRIDE + d0 + j0), b3 = ld4(Ls + (d0 + m0 + 3) * LSTRIDE + d0 + j0);
+                fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
+            }
+            *reinterpret_cast<float4*>(Ls + (d0 + 16 + i) * LSTRIDE + d0 + j0) =
+                make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
+        }
+        sync();
+        // D: X[512:1536] = T_[32:,32:] L_[32:,:32]   (32x32, stride 32)
+        {
+            const int i = tid >> 3, j0 = (tid & 7) * 4;
+            float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+            const float* trow = Ls + (32 + i) * LSTRIDE + 32;
+            const int mend = (i + 4) & ~3;  // T_[32:,32:][i][m] = 0 for m > i
+    #pragma unroll 2
+            for (int m0 = 0; m0 < mend; m0 += 4) {
+                const float4 t4 = ld4(trow + m0);
+                const float4 b0 = ld4(Ls + (32 + m0) * LSTRIDE + j0), b1 = ld4(Ls + (33 + m0) * LSTRIDE + j0);
+                const float4 b2 = ld4(Ls + (34 + m0) * LSTRIDE + j0), b3 = ld4(Ls + (35 + m0) * LSTRIDE + j0);
+                fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
+            }
+            *reinterpret_cast<float4*>(X + 512 + i * 32 + j0) =
+                make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
+        }
+        sync();
+        // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j)
+        {
+            const int i = tid >> 3, j0 = (tid & 7) * 4;
+            float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+            const float* xrow = X + 512 + i * 32;
+    #pragma unroll 2
+            for (int m0 = j0; m0 < 32; m0 += 4) {
+                const float4 x4 = ld4(xrow + m0);
+                const float4 b0 = ld4(Ls + m0 * LSTRIDE + j0), b1 = ld4(Ls + (m0 + 1) * LSTRIDE + j0);
+                const float4 b2 = ld4(Ls + (m0 + 2) * LSTRIDE + j0), b3 = ld4(Ls + (m0 + 3) * LSTRIDE + j0);
+                fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
+            }
+            *reinterpret_cast<float4*>(Ls + (32 + i) * LSTRIDE + j0) =
+                make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
+        }
+        sync();
     }
-    sync();
 }
 
 }  // namespace gdn

@@ -66,7 +66,7 @@ constexpr uint32_t OFF_TPP_HI = OFF_X + 16384;  //  T'' = T diag(beta e^c)    [6
 constexpr uint32_t OFF_TPP_LO = OFF_X + 24576;
 constexpr uint32_t OFF_W_HI = OFF_X + 32768;    //  W^T [128 dk][64 tok] (MN-major B operand)
 constexpr uint32_t OFF_W_LO = OFF_X + 49152;    //  (must follow W_HI by 16 KB: stacked along N)
-constexpr uint32_t OFF_XTMP = OFF_X + 0;        //  inversion products P (fp32, 6 KB)
+constexpr uint32_t OFF_XTMP = OFF_X + 0;        //  inversion products (fp32, 4.5 KB)
 constexpr uint32_t OFF_M_HI = 131072;    // M = scale (q k^T) * decay, [64][64] bf16
 constexpr uint32_t OFF_M_LO = 139264;
 constexpr uint32_t OFF_L = 147456;       // L / T fp32 [64][68]; o staging afterwards (8 KB/panel)
@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
             }
         };
-        invert_unit_lower(Ls, X, tid, gate_work, [] { __syncthreads(); });
+        invert_unit_lower<true>(Ls, X, tid, gate_work, [] { __syncthreads(); });
         if (rec) {
             for (int e = tid; e < CS * CS; e += NTHREADS) rec[DBG_T + e] = Ls[(e >> 6) * LSTRIDE + (e & 63)];
             if (tid < CS) rec[DBG_C + tid] = c_s[tid];

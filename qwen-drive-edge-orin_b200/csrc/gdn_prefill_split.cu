@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 }
                 ptx::tc_fence_before();
                 csync();
-                invert_unit_lower(Ls, X, tid, [](int) {}, csync);
+                invert_unit_lower<false>(Ls, X, tid, [](int) {}, csync);
                 {   // T' -> staging (stacked hi/lo), T'' -> local
                     const int i = tid >> 2, jb = tid & 3;
                     float tp[16], tpp[16];

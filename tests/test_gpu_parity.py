@@ -356,7 +356,10 @@ def test_prefill_then_decode_continues_the_sequence():
                                            (1, 1141, 16, 32, True), (3, 300, 4, 8, True)])
 def test_split_and_fused_kernels_agree(B, T, HQK, HV, s0, monkeypatch):
     """The cluster-split kernel (prep CTAs feeding a chain CTA) and the one-CTA kernel compute the same
-    prefill: each against the oracle, and against each other."""
+    prefill: each against the oracle, and against each other. They share operand layouts and the
+    precision scheme but not the triangular inverse's block products (tf32x3 tensor-core tiles in the
+    one-CTA kernel, fp32 CUDA-core products in the split kernel), so they agree to within rounding of
+    those products, far inside the oracle tolerances, rather than bit for bit."""
     inp = make_inputs(B, T, HQK, HV, 128, seed=3000 + T + B, dist="baseline", with_s0=s0)
     o_ref, sf_ref = O.chunk_gated_delta_rule(inp.q, inp.k, inp.v, inp.g, inp.beta, 64, inp.s0)
     y_ref = O.gated_rmsnorm(o_ref, inp.z, inp.w, inp.eps)
@@ -369,6 +372,7 @@ def test_split_and_fused_kernels_agree(B, T, HQK, HV, s0, monkeypatch):
         check_y(y, y_ref, f"{kern}-y B{B} T{T}")
         assert np.array_equal(sf, sf2)
         res[kern] = (o, sf, y)
-    assert np.array_equal(res["fused"][0], res["split"][0]) and np.array_equal(res["fused"][1], res["split"][1])
+    assert max_abs(res["fused"][0], res["split"][0]) <= O_MAX_ABS / 4
+    assert tensor_l2_rel(res["fused"][1], res["split"][1]) <= 1e-4
     assert max_rel(res["fused"][2], res["split"][2]) < Y_MAX_REL
     assert gdn_b200.binding.read_status() == 0
