@@ -303,6 +303,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 128, 0, 1, 1);  // -S^T [W_hi^T | W_lo^T]  (A in TMEM, B MN-major)
     constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T q^T, v_new^T M^T (A in TMEM)
     constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K   (A in TMEM, B MN-major)
+    // shared-memory descriptors (SW128, SBO 1024) by byte offset from sb, one per LBO
+    const uint32_t dlo16 = ptx::sw128_desc_lo(sb, 16), dlo8k = ptx::sw128_desc_lo(sb, 8192),
+                   dlo16k = ptx::sw128_desc_lo(sb, 16384);
+    auto desc = [](uint32_t lo_base, uint32_t off) { return ptx::desc_pair(lo_base + (off >> 4), ptx::sw128_desc_hi(1024)); };
 
     for (int n = 0; n < NC; ++n) {
         if (*abort_flag) break;
@@ -373,8 +377,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
             for (int s = 0; s < 8; ++s) {
                 const uint32_t koff = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
-                const uint64_t a = ptx::sw128_desc(sb + OFF_QK + koff, 16, 1024);
-                const uint64_t b = ptx::sw128_desc(sb + OFF_QK + 8192 + koff, 16, 1024);
+                const uint64_t a = desc(dlo16, OFF_QK + koff);
+                const uint64_t b = desc(dlo16, OFF_QK + 8192 + koff);
                 ptx::mma_bf16(tmem + TM_P, a, b, ID_P, s > 0);
             }
             commit();
@@ -491,8 +495,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ptx::tc_fence_after();
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
-                const uint64_t a = ptx::sw128_desc(sb + OFF_QK + 8192 + s * 2048, 16384, 1024);
-                const uint64_t b = ptx::sw128_desc(sb + OFF_TPP_HI + s * 32, 16, 1024);  // 128 rows: hi then lo
+                const uint64_t a = desc(dlo16k, OFF_QK + 8192 + s * 2048);
+                const uint64_t b = desc(dlo16, OFF_TPP_HI + s * 32);  // 128 rows: hi then lo
                 ptx::mma_bf16(tmem + TM_W, a, b, ID_W, s > 0);
             }
             commit();
@@ -543,8 +547,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             // cols 0-63 accumulate the hi terms, cols 64-127 the lo terms (B stacked along N)
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
-                const uint64_t a = ptx::sw128_desc(sb + OFF_V + s * 2048, 8192, 1024);
-                const uint64_t b = ptx::sw128_desc(sb + OFF_TP_HI + s * 32, 16, 1024);  // [T'_hi; T'_lo]
+                const uint64_t a = desc(dlo8k, OFF_V + s * 2048);
+                const uint64_t b = desc(dlo16, OFF_TP_HI + s * 32);  // [T'_hi; T'_lo]
                 ptx::mma_bf16(tmem + TM_V, a, b, ID_U, s > 0);
             }
             // S_hi [W_hi | W_lo], S_lo [W_hi | W_lo]; S^T from TMEM, W^T tiles MN-major (LBO = 16 KB)
@@ -553,7 +557,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
-                    const uint64_t b = ptx::sw128_desc(sb + OFF_W_HI + s * 2048, 16384, 1024);
+                    const uint64_t b = desc(dlo16k, OFF_W_HI + s * 2048);
                     ptx::mma_bf16_ts(tmem + TM_V, tmem + sa + 8 * s, b, ID_WS, 1u);
                 }
             }
@@ -605,7 +609,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
-                    const uint64_t b = ptx::sw128_desc(sb + OFF_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
+                    const uint64_t b = desc(dlo16, OFF_QK + (s >> 2) * 16384 + (s & 3) * 32);
                     ptx::mma_bf16_ts(tmem + TM_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
                 }
             }
@@ -616,7 +620,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint32_t mb = (term == 2) ? OFF_M_LO : OFF_M_HI;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const uint64_t b = ptx::sw128_desc(sb + mb + s * 32, 16, 1024);
+                    const uint64_t b = desc(dlo16, mb + s * 32);
                     ptx::mma_bf16_ts(tmem + TM_O2, tmem + va + 8 * s, b, ID_O, (term | s) > 0);
                 }
             }
@@ -625,7 +629,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint32_t va = part ? TM_VP_LO : TM_VP_HI;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const uint64_t b = ptx::sw128_desc(sb + OFF_QK + 8192 + s * 2048, 16384, 1024);
+                    const uint64_t b = desc(dlo16k, OFF_QK + 8192 + s * 2048);
                     ptx::mma_bf16_ts(tmem + TM_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
                 }
             }

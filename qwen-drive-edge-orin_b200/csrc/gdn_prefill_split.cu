@@ -255,6 +255,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 128, 0, 1, 1);
     constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);
     constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);
+    // shared-memory descriptors (SW128, SBO 1024) by byte offset from sb, one per LBO
+    const uint32_t dlo16 = ptx::sw128_desc_lo(sb, 16), dlo8k = ptx::sw128_desc_lo(sb, 8192),
+                   dlo16k = ptx::sw128_desc_lo(sb, 16384);
+    auto desc = [](uint32_t lo_base, uint32_t off) { return ptx::desc_pair(lo_base + (off >> 4), ptx::sw128_desc_hi(1024)); };
 
     auto aslot = [](int m) { return C_ASLOT + (uint32_t)(m % NSLOT) * ASLOT; };
     auto bslot = [](int m) { return C_BSLOT + (uint32_t)(m % NSLOT) * B_BYTES; };
@@ -426,8 +430,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 #pragma unroll
                     for (int s = 0; s < 8; ++s) {
                         const uint32_t koff = (uint32_t)(s >> 2) * 16384u + (uint32_t)(s & 3) * 32u;
-                        const uint64_t a = ptx::sw128_desc(sb + P_QK + koff, 16, 1024);
-                        const uint64_t b = ptx::sw128_desc(sb + P_QK + 8192 + koff, 16, 1024);
+                        const uint64_t a = desc(dlo16, P_QK + koff);
+                        const uint64_t b = desc(dlo16, P_QK + 8192 + koff);
                         ptx::mma_bf16(tmem + T_P, a, b, ID_P, s > 0);
                     }
                     commit();
@@ -503,8 +507,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ptx::tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
-                        const uint64_t a = ptx::sw128_desc(sb + P_QK + 8192 + s * 2048, 16384, 1024);
-                        const uint64_t b = ptx::sw128_desc(sb + P_TPP + s * 32, 16, 1024);
+                        const uint64_t a = desc(dlo16k, P_QK + 8192 + s * 2048);
+                        const uint64_t b = desc(dlo16, P_TPP + s * 32);
                         ptx::mma_bf16(tmem + T_W, a, b, ID_W, s > 0);
                     }
                     commit();
@@ -716,19 +720,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ptx::tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
-                        const uint64_t a = ptx::sw128_desc(sb + C_V + s * 2048, 8192, 1024);
-                        const uint64_t b = ptx::sw128_desc(sb + sp + A_TP + s * 32, 16, 1024);
+                        const uint64_t a = desc(dlo8k, C_V + s * 2048);
+                        const uint64_t b = desc(dlo16, sp + A_TP + s * 32);
                         ptx::mma_bf16(tmem + T_C12, a, b, ID_U, s > 0);
                     }
                     commit_to(B_VT);      // the v tile is free once these have run
                     wait_bar(B_SOP, ph);  // S_n^T hi/lo in TMEM
                     ptx::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
                         const uint32_t sa = part ? T_SA_LO : T_SA_HI;
 #pragma unroll
                         for (int s = 0; s < 8; ++s) {
-                            const uint64_t b = ptx::sw128_desc(sb + sp + A_W + s * 2048, 16384, 1024);
+                            const uint64_t b = desc(dlo16k, sp + A_W + s * 2048);
                             ptx::mma_bf16_ts(tmem + T_C12, tmem + sa + 8 * s, b, ID_WS, 1u);
                         }
                     }
@@ -737,12 +741,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     wait_bar(B_K, ph);
                     wait_bar(B_VNR, ph);
                     ptx::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
                         const uint32_t va = part ? T_VP_LO : T_VP_HI;
 #pragma unroll
                         for (int s = 0; s < 4; ++s) {
-                            const uint64_t b = ptx::sw128_desc(sb + C_QK + 8192 + s * 2048, 16384, 1024);
+                            const uint64_t b = desc(dlo16k, C_QK + 8192 + s * 2048);
                             ptx::mma_bf16_ts(tmem + T_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
                         }
                     }
@@ -764,12 +768,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     wait_bar(B_Q, ph);
                     if (n > 0) wait_bar(B_OFREE, (uint32_t)((n - 1) & 1));
                     ptx::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
                         const uint32_t sa = part ? T_SA_LO : T_SA_HI;
 #pragma unroll
                         for (int s = 0; s < 8; ++s) {
-                            const uint64_t b = ptx::sw128_desc(sb + C_QK + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
+                            const uint64_t b = desc(dlo16, C_QK + (s >> 2) * 16384 + (s & 3) * 32);
                             ptx::mma_bf16_ts(tmem + T_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
                         }
                     }
@@ -780,13 +784,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     if (!ptx::mbar_wait(bar(B_FULLB + n % NSLOT), slot_par(n), WAIT_ITERS)) fail();
                     ptx::tc_fence_after();
                     const uint32_t bp = bslot(n);
-#pragma unroll
+#pragma unroll 1
                     for (int term = 0; term < 3; ++term) {
                         const uint32_t va = (term == 1) ? T_VN_LO : T_VN_HI;
                         const uint32_t mb = bp + ((term == 2) ? 8192u : 0u);
 #pragma unroll
                         for (int s = 0; s < 4; ++s) {
-                            const uint64_t b = ptx::sw128_desc(sb + mb + s * 32, 16, 1024);
+                            const uint64_t b = desc(dlo16, mb + s * 32);
                             ptx::mma_bf16_ts(tmem + T_O2, tmem + va + 8 * s, b, ID_O, (term | s) > 0);
                         }
                     }

@@ -271,6 +271,24 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t start, uint32_t lbo, uin
     return d;
 }
 
+// The same descriptor as two 32-bit words, for base + offset addressing in unrolled MMA
+// loops: low word ((start >> 4) & 0x3FFF) | (lbo >> 4) << 16, high word sbo, version and
+// layout. The field keeps address bits 4-17; a CTA's shared memory spans less than 256 KB
+// above a base whose bits 4-17 the mask keeps, so adding a 16-byte-multiple offset below
+// that span to the low word does not carry into the lbo field. Each descriptor then costs
+// one integer add instead of a shift-mask-or sequence.
+__host__ __device__ constexpr uint32_t sw128_desc_hi(uint32_t sbo) {
+    return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+__device__ __forceinline__ uint32_t sw128_desc_lo(uint32_t start, uint32_t lbo) {
+    return ((start >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+__device__ __forceinline__ uint64_t desc_pair(uint32_t lo, uint32_t hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+
 // Instruction descriptor, kind::f16: bf16 A/B, fp32 D.
 //   a_mn / b_mn : operand is MN-major (1) or K-major (0); neg_a negates A.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_mn, int neg_a) {
