@@ -5,14 +5,14 @@
 //   * rank 0, the chain CTA, owns the recurrent state and runs only the
 //     state-dependent steps of every chunk: C12 (v_new), C3/C4 (output and
 //     state increment) and the state update, and stages o as bf16;
-//   * ranks 1..NP, the prep CTAs, run the state-independent chunk math for
-//     chunks n = rank-1, rank-1+NP, ...: gates, P1 ([Q;K]K^T), L and M, the
+//   * ranks 2..NP+1, the prep CTAs, run the state-independent chunk math for
+//     chunks n = rank-2, rank-2+NP, ...: gates, P1 ([Q;K]K^T), L and M, the
 //     triangular inverse, T' and T'', P3 (W), and ship them into the chain
 //     CTA's slot buffers with shared-to-shared bulk copies (completing on the
 //     chain's mbarriers; no multicast). A slot has two parts that are handed
 //     back separately: part A (T', W, decay factors) once C12 has read it,
 //     part B (M) once the intra-chunk output term has;
-//   * rank NP+1, the output CTA, receives each chunk's staged o the same way
+//   * rank 1, the output CTA, receives each chunk's staged o the same way
 //     and runs the gated-RMSNorm epilogue (z tiles, norm weight, y stores).
 // Prep, chain and output work of different chunks overlap, so the chain's
 // period per chunk is its own work only.
@@ -53,7 +53,12 @@ constexpr int LAUNCH_REGS = 168, COMPUTE_REGS = 192, ISSUE_REGS = 120;
 static_assert(2 * 128 * COMPUTE_REGS + 128 * ISSUE_REGS <= NTHREADS * LAUNCH_REGS, "register split exceeds the pool");
 constexpr uint32_t CSYNC = 1;            // named barrier of warps 0-7
 constexpr int NP = 2;                    // prep CTAs per cluster
-constexpr uint32_t OUT_RANK = NP + 1;    // the output CTA
+// Cluster ranks 2r and 2r+1 land on neighbouring SMs (one TPC). The kernel is sensitive to
+// instruction fetch (its hot loops exceed an SM's instruction cache), and it ran faster
+// with the two prep CTAs (the same code) on one pair and the chain and output CTAs on the
+// other than with the chain and a prep CTA paired (config 1: 83.3 -> 80.0 us).
+constexpr uint32_t OUT_RANK = 1;         // the output CTA
+constexpr uint32_t PREP_RANK0 = 2;       // prep CTAs: ranks 2 .. NP + 1
 constexpr int CLUSTER = NP + 2;          // chain, NP prep CTAs, output
 
 // ---- prep CTA staging layout (one chunk's shipment)
@@ -403,7 +408,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             }
         } else if (!outcta) {
             // ---------------- prep CTA
-            const int pi = (int)rank - 1;  // owns chunks pi, pi + NP, ...
+            const int pi = (int)rank - (int)PREP_RANK0;  // owns chunks pi, pi + NP, ...
             float* Ls = reinterpret_cast<float*>(smem + P_L);
             if (tid == 0 && pi < NC) {
                 load_q(pi);
@@ -681,7 +686,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         const bool mma_out = chain && warp == ISSUER_WARP + 2;
         const bool gate_warp = !chain && !outcta && warp == ISSUER_WARP;
         auto prep_bar = [&](int b, int m) {  // the prep CTAs' barriers sit at their own misc offset
-            return ptx::mapa(sb + P_MISC + M_BAR + 8u * (uint32_t)b, (uint32_t)(1 + m % NSLOT));
+            return ptx::mapa(sb + P_MISC + M_BAR + 8u * (uint32_t)b, (uint32_t)(PREP_RANK0 + m % NSLOT));
         };
         auto arm_slot = [&](int b, int m, uint32_t bytes) {
             const bool odd = (m % NSLOT) != 0;
@@ -841,7 +846,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // ---------------- prep CTA: in-chunk cumulative log-decay c (warp scan, lane l holds
             // tokens 2l and 2l+1), beta, e^c and e^{cL-c} of this CTA's chunks, up to two chunks
             // ahead of warps 0-7, so that none of it (global loads included) is on their path.
-            const int pi = (int)rank - 1;
+            const int pi = (int)rank - (int)PREP_RANK0;
             int k = 0;
             for (int n = pi; n < NC; n += NP, ++k) {
                 if (*abort_flag) break;
