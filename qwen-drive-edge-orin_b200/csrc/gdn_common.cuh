@@ -108,10 +108,53 @@ constexpr float LOG2E = 1.4426950408889634f;
 
 // Split two fp32 values into packed bf16 hi parts and packed bf16 lo parts
 // (x = hi + lo to ~16 mantissa bits).
+// ---------------------------------------------------------------------------
+// Packed fp32 pairs: sm_100 runs add / mul / fma on the two fp32 halves of a 64-bit
+// register pair in one instruction (PTX .f32x2, round-to-nearest like the scalar forms),
+// which halves the instruction count of the element-wise steps.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// bf16 hi/lo split of two values: hi = bf16(x), lo = bf16(x - hi).
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = pack_bf16(a - __low2float(h), b - __high2float(h));
+}
+// The same split with the two residuals in one packed subtraction (fewer instructions,
+// but the packed operands want register pairs: for code with registers to spare).
+__device__ __forceinline__ void split2x(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    float ra, rb;
+    f2_unpack(f2_sub(f2_pack(a, b), f2_pack(__uint_as_float(hi << 16), __uint_as_float(hi & 0xFFFF0000u))), ra, rb);
+    lo = pack_bf16(ra, rb);
 }
 
 // Write 8 consecutive fp32 values as bf16 hi (and optionally lo) parts into a
@@ -120,7 +163,7 @@ __device__ __forceinline__ void put8_split(uint32_t hi_addr, uint32_t lo_addr, c
                                            bool want_lo) {
     uint32_t h[4], l[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) split2(x[2 * i], x[2 * i + 1], h[i], l[i]);
+    for (int i = 0; i < 4; ++i) split2x(x[2 * i], x[2 * i + 1], h[i], l[i]);
     st_shared_v4(hi_addr, h[0], h[1], h[2], h[3]);
     if (want_lo) st_shared_v4(lo_addr, l[0], l[1], l[2], l[3]);
 }

@@ -324,17 +324,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         ptx::tmem_ld32(tl + T_C12 + 64 + 32 * half, v2);
                         ptx::tmem_wait_ld();
 #pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
+                        for (int jj = 0; jj < 32; jj += 2)
+                            f2_unpack(f2_add(f2_pack(v[jj], v[jj + 1]), f2_pack(v2[jj], v2[jj + 1])), v[jj], v[jj + 1]);
                     }
                     uint32_t vh[16], vl[16], ph_[16], pl[16];
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 e4 = ld4(ed_s + 32 * half + 4 * j4);
                         const int j = 2 * j4;
-                        split2(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
-                        split2(v[2 * j + 2], v[2 * j + 3], vh[j + 1], vl[j + 1]);
-                        split2(v[2 * j] * e4.x, v[2 * j + 1] * e4.y, ph_[j], pl[j]);
-                        split2(v[2 * j + 2] * e4.z, v[2 * j + 3] * e4.w, ph_[j + 1], pl[j + 1]);
+                        float w0, w1, w2, w3;
+                        f2_unpack(f2_mul(f2_pack(v[2 * j], v[2 * j + 1]), f2_pack(e4.x, e4.y)), w0, w1);
+                        f2_unpack(f2_mul(f2_pack(v[2 * j + 2], v[2 * j + 3]), f2_pack(e4.z, e4.w)), w2, w3);
+                        split2x(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
+                        split2x(v[2 * j + 2], v[2 * j + 3], vh[j + 1], vl[j + 1]);
+                        split2x(w0, w1, ph_[j], pl[j]);
+                        split2x(w2, w3, ph_[j + 1], pl[j + 1]);
                     }
                     if (tid < CS) ecl[(n & 1) * CS + tid] = reinterpret_cast<const float*>(smem + sp + A_EC)[tid];
                     // the previous chunk's v_new^T M^T and dS have read these columns (Y and X1 waited)
