@@ -490,15 +490,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     const int i = tid >> 2, jb = tid & 3;
                     float tp[16], tpp[16];
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
+                    for (int q4 = 0; q4 < 4; ++q4) {  // T' = T diag(beta), T'' = T' diag(e^c), two columns per step
                         const float4 t4 = ld4(Ls + i * LSTRIDE + 16 * jb + 4 * q4);
-                        const float tt[4] = {t4.x, t4.y, t4.z, t4.w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int jj = 4 * q4 + u, j = 16 * jb + jj;
-                            tp[jj] = tt[u] * beta_s[j];
-                            tpp[jj] = tp[jj] * ec_s[j];
-                        }
+                        const float4 b4 = ld4(beta_s + 16 * jb + 4 * q4), e4 = ld4(ec_s + 16 * jb + 4 * q4);
+                        const int jj = 4 * q4;
+                        const uint64_t p0 = f2_mul(f2_pack(t4.x, t4.y), f2_pack(b4.x, b4.y));
+                        const uint64_t p1 = f2_mul(f2_pack(t4.z, t4.w), f2_pack(b4.z, b4.w));
+                        f2_unpack(p0, tp[jj], tp[jj + 1]);
+                        f2_unpack(p1, tp[jj + 2], tp[jj + 3]);
+                        f2_unpack(f2_mul(p0, f2_pack(e4.x, e4.y)), tpp[jj], tpp[jj + 1]);
+                        f2_unpack(f2_mul(p1, f2_pack(e4.z, e4.w)), tpp[jj + 2], tpp[jj + 3]);
                     }
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
@@ -534,7 +535,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ptx::tmem_ld32(tl + T_W + 64 + 32 * half, v2);
                     ptx::tmem_wait_ld();
 #pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
+                    for (int jj = 0; jj < 32; jj += 2)
+                        f2_unpack(f2_add(f2_pack(v[jj], v[jj + 1]), f2_pack(v2[jj], v2[jj + 1])), v[jj], v[jj + 1]);
 #pragma unroll
                     for (int ch = 0; ch < 4; ++ch) {
                         const uint32_t co = sw_chunk(row, 4 * half + ch, 128);
