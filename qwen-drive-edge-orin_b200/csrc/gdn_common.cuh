@@ -180,8 +180,8 @@ __device__ __forceinline__ void put8_split(uint32_t hi_addr, uint32_t lo_addr, c
 //     operands split in two tf32 terms (a = a_hi + a_lo; a b ~ a_hi b_hi + a_hi b_lo +
 //     a_lo b_hi, the "3xTF32" scheme, about fp32 accuracy), one 16x8 output tile per
 //     warp; X holds 1152 floats (rows of 36, conflict-free fragment loads).
-//   kTensorProducts = false: CUDA-core products register-blocked 1x4 with 16-byte
-//     loads; X holds 1536 floats.
+//   kTensorProducts = false: CUDA-core products with 16-byte loads, register-blocked 1x4
+//     (B-D) and 2x4 (E); X holds 2624 floats.
 // Both skip the tiles or terms that the triangular factors make zero.
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
@@ -362,7 +362,7 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
                 make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
         }
         sync();
-        // D: X[512:1536] = T_[32:,32:] L_[32:,:32]   (32x32, stride 32)
+        // D: X2 = T_[32:,32:] L_[32:,:32], stored transposed: X2T[j][i] at X[512 + 34 j + i]
         {
             const int i = tid >> 3, j0 = (tid & 7) * 4;
             float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
@@ -375,24 +375,52 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
                 const float4 b2 = ld4(Ls + (34 + m0) * LSTRIDE + j0), b3 = ld4(Ls + (35 + m0) * LSTRIDE + j0);
                 fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
             }
-            *reinterpret_cast<float4*>(X + 512 + i * 32 + j0) =
-                make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
+            float* xt = X + 512 + i;
+            xt[(j0 + 0) * 34] = acc0.x + acc1.x;
+            xt[(j0 + 1) * 34] = acc0.y + acc1.y;
+            xt[(j0 + 2) * 34] = acc0.z + acc1.z;
+            xt[(j0 + 3) * 34] = acc0.w + acc1.w;
         }
         sync();
-        // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j)
+        // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j). A thread takes a
+        // 2x4 tile (rows 2rp, 2rp+1, columns 4cg..4cg+3) over half of the m range (threads
+        // 128-255 the upper half, their partial sums handed over in X[1600 + 8t]); each warp
+        // starts at the first m where its two column groups of T can be nonzero (warp-uniform),
+        // and the zeros of T above the diagonal make the rest of the range exact. The 2x4 tiles
+        // load a third of the shared-memory bytes per product of the 1x4 form, which bounded
+        // this stage.
         {
-            const int i = tid >> 3, j0 = (tid & 7) * 4;
-            float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-            const float* xrow = X + 512 + i * 32;
-    #pragma unroll 2
-            for (int m0 = j0; m0 < 32; m0 += 4) {
-                const float4 x4 = ld4(xrow + m0);
-                const float4 b0 = ld4(Ls + m0 * LSTRIDE + j0), b1 = ld4(Ls + (m0 + 1) * LSTRIDE + j0);
-                const float4 b2 = ld4(Ls + (m0 + 2) * LSTRIDE + j0), b3 = ld4(Ls + (m0 + 3) * LSTRIDE + j0);
-                fma4(acc0, x4.x, b0); fma4(acc1, x4.y, b1); fma4(acc0, x4.z, b2); fma4(acc1, x4.w, b3);
+            const int kh = tid >> 7, t = tid & 127, rp = t & 15, cg = t >> 4, i0 = 2 * rp, j0 = 4 * cg;
+            const int wq = t >> 5;                                // column groups 2wq, 2wq + 1
+            const int mlo = kh ? (wq > 2 ? 8 * wq : 16) : 8 * wq, mhi = 16 * kh + 16;
+            float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, c0 = a0, c1 = a0;
+            for (int mb = mlo; mb < mhi; mb += 8) {               // 0, 1 or 2 blocks of 8, warp-uniform
+                const float* xb = X + 512 + mb * 34 + i0;
+                const float* tb = Ls + mb * LSTRIDE + j0;
+    #pragma unroll
+                for (int m = 0; m < 8; m += 2) {
+                    const float2 x0 = *reinterpret_cast<const float2*>(xb + m * 34);
+                    const float2 x1 = *reinterpret_cast<const float2*>(xb + (m + 1) * 34);
+                    const float4 t0 = ld4(tb + m * LSTRIDE), t1 = ld4(tb + (m + 1) * LSTRIDE);
+                    fma4(a0, x0.x, t0); fma4(a1, x0.y, t0);
+                    fma4(c0, x1.x, t1); fma4(c1, x1.y, t1);
+                }
             }
-            *reinterpret_cast<float4*>(Ls + (32 + i) * LSTRIDE + j0) =
-                make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
+            a0 = make_float4(a0.x + c0.x, a0.y + c0.y, a0.z + c0.z, a0.w + c0.w);
+            a1 = make_float4(a1.x + c1.x, a1.y + c1.y, a1.z + c1.z, a1.w + c1.w);
+            float* part = X + 1600 + 8 * t;
+            if (kh) {
+                *reinterpret_cast<float4*>(part) = a0;
+                *reinterpret_cast<float4*>(part + 4) = a1;
+            }
+            sync();
+            if (!kh) {
+                const float4 b0 = ld4(part), b1 = ld4(part + 4);
+                *reinterpret_cast<float4*>(Ls + (32 + i0) * LSTRIDE + j0) =
+                    make_float4(-(a0.x + b0.x), -(a0.y + b0.y), -(a0.z + b0.z), -(a0.w + b0.w));
+                *reinterpret_cast<float4*>(Ls + (33 + i0) * LSTRIDE + j0) =
+                    make_float4(-(a1.x + b1.x), -(a1.y + b1.y), -(a1.z + b1.z), -(a1.w + b1.w));
+            }
         }
         sync();
     }
