@@ -306,10 +306,55 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 hand_off(B_SOP);
             }
             float* ecl = misc + M_C / 4;  // e^c of chunks with even / odd index
-            for (int n = 0; n < NC; ++n) {
+            // ---- o(m) = scale e^c o1 + o2 -> bf16 staging buffer (chunk parity). Staged transposed,
+            //      o^T [128 dv][64 tok] with 128-byte rows in 16-byte chunks XOR-swizzled by (dv & 7):
+            //      one thread writes its row half with four 16-byte stores. Runs at the top of chunk
+            //      m + 1's iteration, under the wait for C12(m + 1), so that it is off the recurrence.
+            auto stage_output = [&](int m) {
+                wait_bar(B_Y, (uint32_t)(m & 1));
+                ptx::tc_fence_after();
+                // the output CTA has handed back this buffer (its chunk m - 2)
+                if (m >= 2 && !ptx::mbar_wait(bar(B_EMPTYO + (m & 1)), (uint32_t)(((m >> 1) - 1) & 1), WAIT_ITERS))
+                    fail();
+                const float* ecm = ecl + (m & 1) * CS;
+                const uint32_t ob = sb + C_OST + (uint32_t)(m & 1) * O_BYTES;
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {  // 16 columns at a time (registers: the state is live)
+                    float v[16], v2[16];
+                    ptx::tmem_ld16(tl + T_O + 32 * half + 16 * h2, v);
+                    ptx::tmem_ld16(tl + T_O2 + 32 * half + 16 * h2, v2);
+                    ptx::tmem_wait_ld();
+                    if (h2 == 1) hand_off(B_OFREE);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) v[jj] = fmaf(p.scale * ecm[32 * half + 16 * h2 + jj], v[jj], v2[jj]);
+#pragma unroll
+                    for (int c = 0; c < 2; ++c)
+                        st_shared_v4(ob + sw_chunk(row, 4 * half + 2 * h2 + c, 128), pack_bf16(v[8 * c], v[8 * c + 1]),
+                                     pack_bf16(v[8 * c + 2], v[8 * c + 3]), pack_bf16(v[8 * c + 4], v[8 * c + 5]),
+                                     pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+                }
+                ptx::fence_proxy_async_smem();  // the staging buffer is read by a bulk copy
+            };
+            // after a barrier of warps 0-7 that follows stage_output(m): thread 0 ships o(m)
+            auto ship_output = [&](int m) {
+                if (tid == 0) {
+                    const uint32_t dst = ptx::mapa(sb + U_OSLOT + (uint32_t)(m & 1) * O_BYTES, OUT_RANK);
+                    const uint32_t fb = ptx::mapa(sb + U_MISC + M_BAR + 8u * (uint32_t)(B_FULLO + (m & 1)), OUT_RANK);
+                    ptx::bulk_copy_s2cluster(dst, sb + C_OST + (uint32_t)(m & 1) * O_BYTES, O_BYTES, fb);
+                }
+            };
+            for (int n = 0; n <= NC; ++n) {  // step NC only stages and ships the last chunk's output
                 if (vote_abort()) break;
                 const uint32_t ph = (uint32_t)(n & 1);
                 const float* ecn = ecl + (n & 1) * CS;
+                if (n > 0) stage_output(n - 1);
+                if (n == NC) {
+                    if (n > 0) {
+                        csync();
+                        ship_output(n - 1);
+                    }
+                    break;
+                }
 
                 // ---- v_new hi/lo and (v_new e^{cL-c}) hi/lo -> TMEM A operands; keep e^c
                 wait_mma(ph);
@@ -349,7 +394,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ptx::tmem_wait_st();
                     hand_off(B_VNR);
                 }
-                csync();  // e^c copied for every thread
+                csync();  // e^c copied for every thread; o(n - 1) staged
+                if (n > 0) ship_output(n - 1);
 
                 // ---- S <- e^{cL} S + dS; the new S^T hi/lo operand (S^T q^T has read the old one)
                 wait_bar(B_X1, ph);
@@ -374,36 +420,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     hand_off(B_SOP);
                 }
 
-                // ---- o = scale e^c o1 + o2 -> bf16 staging buffer (chunk parity) -> output CTA.
-                //      Staged transposed, o^T [128 dv][64 tok] with 128-byte rows in 16-byte chunks
-                //      XOR-swizzled by (dv & 7): one thread writes its row half with four 16-byte stores.
-                wait_bar(B_Y, ph);
-                ptx::tc_fence_after();
-                {
-                    float v[32], v2[32];
-                    ptx::tmem_ld32(tl + T_O + 32 * half, v);
-                    ptx::tmem_ld32(tl + T_O2 + 32 * half, v2);
-                    ptx::tmem_wait_ld();
-                    hand_off(B_OFREE);
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) v[jj] = fmaf(p.scale * ecn[32 * half + jj], v[jj], v2[jj]);
-                    // the output CTA has handed back this buffer (its chunk n - 2)
-                    if (n >= 2 && !ptx::mbar_wait(bar(B_EMPTYO + (n & 1)), (uint32_t)(((n >> 1) - 1) & 1), WAIT_ITERS))
-                        fail();
-                    const uint32_t ob = sb + C_OST + (uint32_t)(n & 1) * O_BYTES;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        st_shared_v4(ob + sw_chunk(row, 4 * half + c, 128), pack_bf16(v[8 * c], v[8 * c + 1]),
-                                     pack_bf16(v[8 * c + 2], v[8 * c + 3]), pack_bf16(v[8 * c + 4], v[8 * c + 5]),
-                                     pack_bf16(v[8 * c + 6], v[8 * c + 7]));
-                }
-                ptx::fence_proxy_async_smem();  // the staging buffer is read by a bulk copy
-                csync();
-                if (tid == 0) {
-                    const uint32_t dst = ptx::mapa(sb + U_OSLOT + (uint32_t)(n & 1) * O_BYTES, OUT_RANK);
-                    const uint32_t fb = ptx::mapa(sb + U_MISC + M_BAR + 8u * (uint32_t)(B_FULLO + (n & 1)), OUT_RANK);
-                    ptx::bulk_copy_s2cluster(dst, sb + C_OST + (uint32_t)(n & 1) * O_BYTES, O_BYTES, fb);
-                }
             }
             if (!*abort_flag) {
                 const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
