@@ -301,6 +301,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     constexpr uint32_t ID_W = ptx::idesc_bf16(128, 128, 1, 0, 0);   // K^T [T''_hi; T''_lo]^T  (A MN-major)
     constexpr uint32_t ID_U = ptx::idesc_bf16(128, 128, 1, 0, 0);   // v^T [T'_hi; T'_lo]^T    (A MN-major)
     constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 128, 0, 1, 1);  // -S^T [W_hi^T | W_lo^T]  (A in TMEM, B MN-major)
+    constexpr uint32_t ID_WS_HI = ptx::idesc_bf16(128, 64, 0, 1, 1);  // -S_lo^T W_hi^T
     constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);    // S^T q^T, v_new^T M^T (A in TMEM)
     constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);   // v_new'^T K   (A in TMEM, B MN-major)
     // shared-memory descriptors (SW128, SBO 1024) by byte offset from sb, one per LBO
@@ -551,14 +552,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint64_t b = desc(dlo16, OFF_TP_HI + s * 32);  // [T'_hi; T'_lo]
                 ptx::mma_bf16(tmem + TM_V, a, b, ID_U, s > 0);
             }
-            // S_hi [W_hi | W_lo], S_lo [W_hi | W_lo]; S^T from TMEM, W^T tiles MN-major (LBO = 16 KB)
+            // S_hi [W_hi | W_lo], then S_lo W_hi (N = 64: the S_lo W_lo term is below the precision
+            // of the split and is left out); S^T from TMEM, W^T tiles MN-major (LBO = 16 KB)
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
                 const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
                     const uint64_t b = desc(dlo16k, OFF_W_HI + s * 2048);
-                    ptx::mma_bf16_ts(tmem + TM_V, tmem + sa + 8 * s, b, ID_WS, 1u);
+                    ptx::mma_bf16_ts(tmem + TM_V, tmem + sa + 8 * s, b, part ? ID_WS_HI : ID_WS, 1u);
                 }
             }
             commit();

@@ -258,6 +258,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     constexpr uint32_t ID_W = ptx::idesc_bf16(128, 128, 1, 0, 0);
     constexpr uint32_t ID_U = ptx::idesc_bf16(128, 128, 1, 0, 0);
     constexpr uint32_t ID_WS = ptx::idesc_bf16(128, 128, 0, 1, 1);
+    constexpr uint32_t ID_WS_HI = ptx::idesc_bf16(128, 64, 0, 1, 1);  // -S_lo^T W_hi^T
     constexpr uint32_t ID_O = ptx::idesc_bf16(128, 64, 0, 0, 0);
     constexpr uint32_t ID_S = ptx::idesc_bf16(128, 128, 0, 1, 0);
     // shared-memory descriptors (SW128, SBO 1024) by byte offset from sb, one per LBO
@@ -756,11 +757,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ptx::tc_fence_after();
 #pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
+                        // S_hi [W_hi | W_lo], then S_lo W_hi (N = 64: the S_lo W_lo term is below
+                        // the precision of the split and is left out)
                         const uint32_t sa = part ? T_SA_LO : T_SA_HI;
+                        const uint32_t idw = part ? ID_WS_HI : ID_WS;
 #pragma unroll
                         for (int s = 0; s < 8; ++s) {
                             const uint64_t b = desc(dlo16k, sp + A_W + s * 2048);
-                            ptx::mma_bf16_ts(tmem + T_C12, tmem + sa + 8 * s, b, ID_WS, 1u);
+                            ptx::mma_bf16_ts(tmem + T_C12, tmem + sa + 8 * s, b, idw, 1u);
                         }
                     }
                     commit();
