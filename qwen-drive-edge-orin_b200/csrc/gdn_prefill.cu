@@ -110,6 +110,9 @@ constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192
               DBG_O = DBG_VN + 8192, DBG_SC = DBG_O + 8192, DBG_REC = DBG_SC + 16384;
 
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
+    // inputs may come from the previous launch in the stream: nothing global is touched before this
+    ptx::grid_dependency_wait();
+    ptx::grid_launch_dependents();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -925,8 +928,20 @@ static cudaError_t launch(const Launch& L) {
     if (!L.dbg && !L.prestage && use_split(L.nseq, L.HV)) return launch_split(p, L.nseq, L.HV, L.stream);
     cudaError_t e = ensure_smem_attr();
     if (e != cudaSuccess) return e;
-    dim3 grid(1, L.HV, L.nseq);
-    gdn_prefill_kernel<<<grid, NTHREADS, SMEM_ALLOC, L.stream>>>(p);
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(1, L.HV, L.nseq);
+    cfg.blockDim = dim3(NTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_ALLOC;
+    cfg.stream = L.stream;
+    // programmatic dependent launch: the kernel waits for the previous grid before touching memory
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gdn_prefill_kernel, p);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -141,6 +141,9 @@ constexpr uint32_t T_VN_HI = 0, T_VN_LO = 32, T_VP_HI = 64, T_VP_LO = 96, T_O = 
 constexpr uint32_t T_P = 0, T_W = 128;
 
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __grid_constant__ Params p) {
+    // inputs may come from the previous launch in the stream: nothing global is touched before this
+    ptx::grid_dependency_wait();
+    ptx::grid_launch_dependents();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -968,13 +971,16 @@ cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream)
     cfg.blockDim = dim3(split::NTHREADS, 1, 1);
     cfg.dynamicSmemBytes = split::SMEM_ALLOC;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = split::CLUSTER;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // programmatic dependent launch: the kernel waits for the previous grid before touching memory
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, split::gdn_prefill_split_kernel, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();

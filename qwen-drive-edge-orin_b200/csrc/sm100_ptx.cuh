@@ -55,6 +55,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     return false;
 }
 
+// Programmatic dependent launch: wait until the grids this launch depends on have completed
+// and their memory is visible (a no-op without such a dependency), then let the next launch
+// in the stream be scheduled: its CTAs take SMs as this grid's CTAs leave them and run up to
+// their own wait while this grid finishes.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Plain arrive on a barrier of this CTA (default release, CTA scope).
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
