@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             for (int c2 = 0; c2 < 2; ++c2) {
                 uint32_t hi[16], lo[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) split2(S[32 * c2 + 2 * j], S[32 * c2 + 2 * j + 1], hi[j], lo[j]);
+                for (int j = 0; j < 16; ++j) split2x(S[32 * c2 + 2 * j], S[32 * c2 + 2 * j + 1], hi[j], lo[j]);
                 ptx::tmem_st16(tl + T_SA_HI + 32 * half + 16 * c2, hi);
                 ptx::tmem_st16(tl + T_SA_LO + 32 * half + 16 * c2, lo);
             }
@@ -366,35 +366,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 {
                     const uint32_t sp = aslot(n);
                     const float* ed_s = reinterpret_cast<const float*>(smem + sp + A_ED);
-                    float v[32];
-                    {
-                        float v2[32];
-                        ptx::tmem_ld32(tl + T_C12 + 32 * half, v);
-                        ptx::tmem_ld32(tl + T_C12 + 64 + 32 * half, v2);
-                        ptx::tmem_wait_ld();
+                    // 16 columns at a time (the state is live in registers)
 #pragma unroll
-                        for (int jj = 0; jj < 32; jj += 2)
-                            f2_unpack(f2_add(f2_pack(v[jj], v[jj + 1]), f2_pack(v2[jj], v2[jj + 1])), v[jj], v[jj + 1]);
-                    }
-                    uint32_t vh[16], vl[16], ph_[16], pl[16];
+                    for (int hq = 0; hq < 2; ++hq) {
+                        float v[16];
+                        {
+                            float v2[16];
+                            ptx::tmem_ld16(tl + T_C12 + 32 * half + 16 * hq, v);
+                            ptx::tmem_ld16(tl + T_C12 + 64 + 32 * half + 16 * hq, v2);
+                            ptx::tmem_wait_ld();
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 e4 = ld4(ed_s + 32 * half + 4 * j4);
-                        const int j = 2 * j4;
-                        float w0, w1, w2, w3;
-                        f2_unpack(f2_mul(f2_pack(v[2 * j], v[2 * j + 1]), f2_pack(e4.x, e4.y)), w0, w1);
-                        f2_unpack(f2_mul(f2_pack(v[2 * j + 2], v[2 * j + 3]), f2_pack(e4.z, e4.w)), w2, w3);
-                        split2x(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
-                        split2x(v[2 * j + 2], v[2 * j + 3], vh[j + 1], vl[j + 1]);
-                        split2x(w0, w1, ph_[j], pl[j]);
-                        split2x(w2, w3, ph_[j + 1], pl[j + 1]);
+                            for (int jj = 0; jj < 16; jj += 2)
+                                f2_unpack(f2_add(f2_pack(v[jj], v[jj + 1]), f2_pack(v2[jj], v2[jj + 1])), v[jj], v[jj + 1]);
+                        }
+                        uint32_t vh[8], vl[8], ph_[8], pl[8];
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 e4 = ld4(ed_s + 32 * half + 16 * hq + 4 * j4);
+                            const int j = 2 * j4;
+                            float w0, w1, w2, w3;
+                            f2_unpack(f2_mul(f2_pack(v[2 * j], v[2 * j + 1]), f2_pack(e4.x, e4.y)), w0, w1);
+                            f2_unpack(f2_mul(f2_pack(v[2 * j + 2], v[2 * j + 3]), f2_pack(e4.z, e4.w)), w2, w3);
+                            split2x(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
+                            split2x(v[2 * j + 2], v[2 * j + 3], vh[j + 1], vl[j + 1]);
+                            split2x(w0, w1, ph_[j], pl[j]);
+                            split2x(w2, w3, ph_[j + 1], pl[j + 1]);
+                        }
+                        // the previous chunk's v_new^T M^T and dS have read these columns (Y and X1 waited)
+                        const uint32_t c0 = 16 * half + 8 * hq;
+                        ptx::tmem_st8(tl + T_VN_HI + c0, vh);
+                        ptx::tmem_st8(tl + T_VN_LO + c0, vl);
+                        ptx::tmem_st8(tl + T_VP_HI + c0, ph_);
+                        ptx::tmem_st8(tl + T_VP_LO + c0, pl);
                     }
                     if (tid < CS) ecl[(n & 1) * CS + tid] = reinterpret_cast<const float*>(smem + sp + A_EC)[tid];
-                    // the previous chunk's v_new^T M^T and dS have read these columns (Y and X1 waited)
-                    ptx::tmem_st16(tl + T_VN_HI + 16 * half, vh);
-                    ptx::tmem_st16(tl + T_VN_LO + 16 * half, vl);
-                    ptx::tmem_st16(tl + T_VP_HI + 16 * half, ph_);
-                    ptx::tmem_st16(tl + T_VP_LO + 16 * half, pl);
                     ptx::tmem_wait_st();
                     hand_off(B_VNR);
                 }
@@ -413,7 +418,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         ptx::tmem_wait_ld();
                         if (c2 == 1) hand_off(B_TSFREE);  // dS read: C12 of the next chunk may start
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
+                        for (int j = 0; j < 32; j += 2)
+                            f2_unpack(f2_fma(f2_pack(gam, gam), f2_pack(S[32 * c2 + j], S[32 * c2 + j + 1]),
+                                             f2_pack(v[j], v[j + 1])),
+                                      S[32 * c2 + j], S[32 * c2 + j + 1]);
                     }
                 }
                 wait_bar(B_X2, ph);  // S^T q^T has read the old state operand
