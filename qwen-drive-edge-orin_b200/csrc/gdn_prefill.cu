@@ -474,15 +474,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             const int i = tid >> 2, jb = tid & 3;
             float tp[16], tpp[16];
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
+            for (int q4 = 0; q4 < 4; ++q4) {  // two columns per packed multiply
                 const float4 t4 = ld4(Ls + i * LSTRIDE + 16 * jb + 4 * q4);
-                const float tt[4] = {t4.x, t4.y, t4.z, t4.w};
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int jj = 4 * q4 + u, j = 16 * jb + jj;
-                    tp[jj] = tt[u] * beta_s[j];
-                    tpp[jj] = tp[jj] * ec_s[j];
-                }
+                const float4 b4 = ld4(beta_s + 16 * jb + 4 * q4), e4 = ld4(ec_s + 16 * jb + 4 * q4);
+                const int jj = 4 * q4;
+                const uint64_t p0 = f2_mul(f2_pack(t4.x, t4.y), f2_pack(b4.x, b4.y));
+                const uint64_t p1 = f2_mul(f2_pack(t4.z, t4.w), f2_pack(b4.z, b4.w));
+                f2_unpack(p0, tp[jj], tp[jj + 1]);
+                f2_unpack(p1, tp[jj + 2], tp[jj + 3]);
+                f2_unpack(f2_mul(p0, f2_pack(e4.x, e4.y)), tpp[jj], tpp[jj + 1]);
+                f2_unpack(f2_mul(p1, f2_pack(e4.z, e4.w)), tpp[jj + 2], tpp[jj + 3]);
             }
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
@@ -512,7 +513,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ptx::tmem_ld32(tl + TM_W + 64 + 32 * half, v2);
             ptx::tmem_wait_ld();
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
+            for (int jj = 0; jj < 32; jj += 2)
+                    f2_unpack(f2_add(f2_pack(v[jj], v[jj + 1]), f2_pack(v2[jj], v2[jj + 1])), v[jj], v[jj + 1]);
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 const uint32_t co = sw_chunk(row, 4 * half + ch, 128);
@@ -578,7 +580,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 ptx::tmem_ld32(tl + TM_V + 64 + 32 * half, v2);
                 ptx::tmem_wait_ld();
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) v[jj] += v2[jj];
+                for (int jj = 0; jj < 32; jj += 2)
+                    f2_unpack(f2_add(f2_pack(v[jj], v[jj + 1]), f2_pack(v2[jj], v2[jj + 1])), v[jj], v[jj + 1]);
             }
             if (rec) {
 #pragma unroll
@@ -587,14 +590,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             {   // v_new hi/lo -> cols [0, 64) (the consumed P1 accumulator)
                 uint32_t vh[16], vl[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) split2(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
+                for (int j = 0; j < 16; ++j) split2x(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
                 ptx::tmem_st16(tl + TM_VN_HI + 16 * half, vh);
                 ptx::tmem_st16(tl + TM_VN_LO + 16 * half, vl);
             }
             uint32_t ph_[16], pl[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                split2(v[2 * j] * ed_s[32 * half + 2 * j], v[2 * j + 1] * ed_s[32 * half + 2 * j + 1], ph_[j], pl[j]);
+            for (int j = 0; j < 16; ++j) {
+                float w0, w1;
+                f2_unpack(f2_mul(f2_pack(v[2 * j], v[2 * j + 1]), f2_pack(ed_s[32 * half + 2 * j], ed_s[32 * half + 2 * j + 1])), w0, w1);
+                split2x(w0, w1, ph_[j], pl[j]);
+            }
             ptx::tc_fence_before();
             __syncthreads();  // every thread has read TM_V before cols [64, 192) are reused
             ptx::tc_fence_after();
