@@ -181,7 +181,7 @@ __device__ __forceinline__ void put8_split(uint32_t hi_addr, uint32_t lo_addr, c
 //     a_lo b_hi, the "3xTF32" scheme, about fp32 accuracy), one 16x8 output tile per
 //     warp; X holds 1152 floats (rows of 36, conflict-free fragment loads).
 //   kTensorProducts = false: CUDA-core products with 16-byte loads, register-blocked 1x4
-//     (B-D) and 2x4 (E); X holds 2624 floats.
+//     (B, C) and 2x4 over split halves of the m range (D, E); X holds 2624 floats.
 // Both skip the tiles or terms that the triangular factors make zero.
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
@@ -362,24 +362,47 @@ __device__ __forceinline__ void invert_unit_lower(float* Ls, float* X, int tid, 
                 make_float4(-(acc0.x + acc1.x), -(acc0.y + acc1.y), -(acc0.z + acc1.z), -(acc0.w + acc1.w));
         }
         sync();
-        // D: X2 = T_[32:,32:] L_[32:,:32], stored transposed: X2T[j][i] at X[512 + 34 j + i]
+        // D: X2 = T_[32:,32:] L_[32:,:32], stored transposed: X2T[j][i] at X[512 + 34 j + i]. A thread
+        // takes a 2x4 tile (rows 2rp, 2rp+1 of T_[32:,32:], columns 4cg..4cg+3) over half of the m
+        // range (threads 128-255 the upper half, partial sums handed over in X[1600 + 8t]); warp w of
+        // a half holds rows 8w..8w+7 and stops where T_[32:,32:] is zero (m > row), warp-uniformly.
         {
-            const int i = tid >> 3, j0 = (tid & 7) * 4;
-            float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
-            const float* trow = Ls + (32 + i) * LSTRIDE + 32;
-            const int mend = (i + 4) & ~3;  // T_[32:,32:][i][m] = 0 for m > i
-    #pragma unroll 2
-            for (int m0 = 0; m0 < mend; m0 += 4) {
-                const float4 t4 = ld4(trow + m0);
-                const float4 b0 = ld4(Ls + (32 + m0) * LSTRIDE + j0), b1 = ld4(Ls + (33 + m0) * LSTRIDE + j0);
-                const float4 b2 = ld4(Ls + (34 + m0) * LSTRIDE + j0), b3 = ld4(Ls + (35 + m0) * LSTRIDE + j0);
-                fma4(acc0, t4.x, b0); fma4(acc1, t4.y, b1); fma4(acc0, t4.z, b2); fma4(acc1, t4.w, b3);
+            const int kh = tid >> 7, t = tid & 127, rp = t >> 3, cg = t & 7, i0 = 2 * rp, j0 = 4 * cg;
+            const int w8 = (t >> 5) * 8;
+            const int mlo = kh ? 16 : 0, mhi = kh ? w8 + 8 : (w8 + 8 < 16 ? w8 + 8 : 16);
+            float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, c0 = a0, c1 = a0;
+            const float* tr0 = Ls + (32 + i0) * LSTRIDE + 32;
+            const float* tr1 = tr0 + LSTRIDE;
+            for (int mb = mlo; mb < mhi; mb += 8) {  // 0, 1 or 2 blocks of 8, warp-uniform
+    #pragma unroll
+                for (int m = 0; m < 8; m += 2) {
+                    const float2 p0 = *reinterpret_cast<const float2*>(tr0 + mb + m);
+                    const float2 p1 = *reinterpret_cast<const float2*>(tr1 + mb + m);
+                    const float4 l0 = ld4(Ls + (32 + mb + m) * LSTRIDE + j0), l1 = ld4(Ls + (33 + mb + m) * LSTRIDE + j0);
+                    fma4(a0, p0.x, l0); fma4(a1, p1.x, l0);
+                    fma4(c0, p0.y, l1); fma4(c1, p1.y, l1);
+                }
             }
-            float* xt = X + 512 + i;
-            xt[(j0 + 0) * 34] = acc0.x + acc1.x;
-            xt[(j0 + 1) * 34] = acc0.y + acc1.y;
-            xt[(j0 + 2) * 34] = acc0.z + acc1.z;
-            xt[(j0 + 3) * 34] = acc0.w + acc1.w;
+            a0 = make_float4(a0.x + c0.x, a0.y + c0.y, a0.z + c0.z, a0.w + c0.w);
+            a1 = make_float4(a1.x + c1.x, a1.y + c1.y, a1.z + c1.z, a1.w + c1.w);
+            float* part = X + 1600 + 8 * t;
+            if (kh) {
+                *reinterpret_cast<float4*>(part) = a0;
+                *reinterpret_cast<float4*>(part + 4) = a1;
+            }
+            sync();
+            if (!kh) {
+                const float4 b0 = ld4(part), b1 = ld4(part + 4);
+                float* xt = X + 512 + i0;
+                xt[(j0 + 0) * 34] = a0.x + b0.x;
+                xt[(j0 + 1) * 34] = a0.y + b0.y;
+                xt[(j0 + 2) * 34] = a0.z + b0.z;
+                xt[(j0 + 3) * 34] = a0.w + b0.w;
+                xt[(j0 + 0) * 34 + 1] = a1.x + b1.x;
+                xt[(j0 + 1) * 34 + 1] = a1.y + b1.y;
+                xt[(j0 + 2) * 34 + 1] = a1.z + b1.z;
+                xt[(j0 + 3) * 34 + 1] = a1.w + b1.w;
+            }
         }
         sync();
         // E: T_[32:,:32] = -X2 T_[:32,:32]   (T_[:32,:32][m][j] = 0 for m < j). A thread takes a
