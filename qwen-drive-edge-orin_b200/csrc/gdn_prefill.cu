@@ -110,6 +110,13 @@ constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192
               DBG_O = DBG_VN + 8192, DBG_SC = DBG_O + 8192, DBG_REC = DBG_SC + 16384;
 
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
+    // the tensor maps are kernel parameters, not data of the previous launch: fetch them while it ends
+    if (threadIdx.x == 0) {
+        ptx::prefetch_tensormap(&p.tm_q);
+        ptx::prefetch_tensormap(&p.tm_k);
+        ptx::prefetch_tensormap(&p.tm_v);
+        if (p.gated) ptx::prefetch_tensormap(&p.tm_z);
+    }
     // inputs may come from the previous launch in the stream: nothing global is touched before this
     ptx::grid_dependency_wait();
     ptx::grid_launch_dependents();
@@ -152,10 +159,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         for (int i = 0; i < 5; ++i) ptx::mbar_init(bar(i), 1);
         ptx::fence_mbar_init();
         *abort_flag = 0;
-        ptx::prefetch_tensormap(&p.tm_q);
-        ptx::prefetch_tensormap(&p.tm_k);
-        ptx::prefetch_tensormap(&p.tm_v);
-        if (p.gated) ptx::prefetch_tensormap(&p.tm_z);
     }
     if (warp == 0) {
         ptx::tmem_alloc(sb + OFF_MISC + MISC_TMEM, TMEM_COLS);

@@ -141,9 +141,13 @@ constexpr uint32_t T_VN_HI = 0, T_VN_LO = 32, T_VP_HI = 64, T_VP_LO = 96, T_O = 
 constexpr uint32_t T_P = 0, T_W = 128;
 
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __grid_constant__ Params p) {
-    // inputs may come from the previous launch in the stream: nothing global is touched before this
-    ptx::grid_dependency_wait();
-    ptx::grid_launch_dependents();
+    // the tensor maps are kernel parameters, not data of the previous launch: fetch them while it ends
+    if (threadIdx.x == 0) {
+        ptx::prefetch_tensormap(&p.tm_q);
+        ptx::prefetch_tensormap(&p.tm_k);
+        ptx::prefetch_tensormap(&p.tm_v);
+        if (p.gated) ptx::prefetch_tensormap(&p.tm_z);
+    }
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -158,19 +162,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     const int h = blockIdx.y;
     const int seq = blockIdx.z;
     const int hq = h / (p.HV / p.HQK);
-
-    int t_begin, len, bcoord;
-    if (p.cu_seqlens != nullptr) {
-        t_begin = p.cu_seqlens[seq];
-        len = p.cu_seqlens[seq + 1] - t_begin;
-        bcoord = 0;
-    } else {
-        t_begin = 0;
-        len = p.T;
-        bcoord = seq;
-    }
-    const int NC = (len + CS - 1) / CS;
-    const long long tok_base = (long long)bcoord * p.T + t_begin;
 
     const uint32_t misc_off = chain ? C_MISC : (outcta ? U_MISC : P_MISC);
     float* misc = reinterpret_cast<float*>(smem + misc_off);
@@ -197,6 +188,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
+    // barriers, TMEM and the tensor maps above touch no global data; inputs may come from the
+    // previous launch in the stream, so everything below waits for it
+    ptx::grid_dependency_wait();
+    ptx::grid_launch_dependents();
+    int t_begin, len, bcoord;
+    if (p.cu_seqlens != nullptr) {
+        t_begin = p.cu_seqlens[seq];
+        len = p.cu_seqlens[seq + 1] - t_begin;
+        bcoord = 0;
+    } else {
+        t_begin = 0;
+        len = p.T;
+        bcoord = seq;
+    }
+    const int NC = (len + CS - 1) / CS;
+    const long long tok_base = (long long)bcoord * p.T + t_begin;
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + misc_off + M_TMEM);
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
 
