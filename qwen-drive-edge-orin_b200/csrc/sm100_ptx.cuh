@@ -50,7 +50,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
 #pragma unroll 1
     for (uint32_t it = 0; it < max_iters; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (it > 512) __nanosleep(32);
+        if (it > 4096) __nanosleep(64);
     }
     return false;
 }
