@@ -77,7 +77,7 @@ constexpr uint32_t MISC_C = 0;      // c        [64] f32
 constexpr uint32_t MISC_BETA = 256; // beta     [64]
 constexpr uint32_t MISC_EC = 512;   // e^c      [64]
 constexpr uint32_t MISC_ED = 768;   // e^{cL-c} [64]
-constexpr uint32_t MISC_BAR = 1024; // 5 mbarriers
+constexpr uint32_t MISC_BAR = 1024; // NBAR mbarriers
 constexpr uint32_t MISC_TMEM = 1088;
 constexpr uint32_t MISC_FLAG = 1092;
 constexpr uint32_t MISC_W = 1152;   // norm weight [128] f32
@@ -91,18 +91,19 @@ static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory 
 constexpr uint32_t TM_P = 0;       // P1 [Q;K]K^T fp32 (64)      -> then v_new^T hi/lo A operands
 constexpr uint32_t TM_VN_HI = 0;   //   v_new^T bf16 pairs (32)
 constexpr uint32_t TM_VN_LO = 32;
-constexpr uint32_t TM_V = 64;      // C12 [hi-part | lo-part] v_new^T fp32 (128) -> then:
-constexpr uint32_t TM_VP_HI = 64;  //   (v_new e^{cL-c})^T hi/lo (64)
+constexpr uint32_t TM_VP_HI = 64;  // (v_new e^{cL-c})^T hi/lo (64)
 constexpr uint32_t TM_VP_LO = 96;
 constexpr uint32_t TM_W = 128;     // P3 [T''_hi | T''_lo] parts of W^T fp32 (128), read before C12
 constexpr uint32_t TM_O = 128;     // C3 S^T q^T (64)
 constexpr uint32_t TM_O2 = 192;    //    v_new^T M^T (64)
-constexpr uint32_t TM_S = 256;     // C4 dS^T fp32 (128)
+constexpr uint32_t TM_S = 256;     // C12 [hi-part | lo-part] v_new^T fp32 (128), then C4 dS^T fp32 (128)
+constexpr uint32_t TM_C12 = TM_S;
 constexpr uint32_t TM_SA_HI = 384; // S^T bf16 pairs, A operand of C12 / C3 (64)
 constexpr uint32_t TM_SA_LO = 448;
 
-// Barrier slots.
-enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4 };
+// Barrier slots: TMA tiles; MMA commit groups (BAR_MMA: every group but the two below, which
+// let the state update start while the output products still run: BAR_DS = dS, BAR_O1 = S^T q^T).
+enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4, BAR_DS = 5, BAR_O1 = 6, NBAR = 7 };
 
 
 // Debug record layout (floats) per (seq, head, chunk).
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     float* X = reinterpret_cast<float*>(smem + OFF_XTMP);
 
     if (tid == 0) {
-        for (int i = 0; i < 5; ++i) ptx::mbar_init(bar(i), 1);
+        for (int i = 0; i < NBAR; ++i) ptx::mbar_init(bar(i), 1);
         ptx::fence_mbar_init();
         *abort_flag = 0;
     }
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                    : (p.prestage ? __half2float(reinterpret_cast<const __half*>(p.w)[tid]) : __bfloat162float(p.w[tid]));
 
     // ---- TMA issue helpers (thread 0) ----
-    uint32_t issued[5] = {0, 0, 0, 0, 0}, consumed[5] = {0, 0, 0, 0, 0};
+    uint32_t issued[NBAR] = {0, 0, 0, 0, 0, 0, 0}, consumed[NBAR] = {0, 0, 0, 0, 0, 0, 0};
     auto load_q = [&](int n) {
         ++issued[BAR_Q];
         ptx::mbar_arrive_expect_tx(bar(BAR_Q), 16384);
@@ -247,17 +248,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         wait_bar(BAR_MMA, consumed[BAR_MMA] & 1u);
         ptx::tc_fence_after();
     };
-    auto commit = [&]() {
-        ptx::mma_commit(bar(BAR_MMA));
-        ++issued[BAR_MMA];
+    auto commit_to = [&](int b) {
+        ptx::mma_commit(bar(b));
+        ++issued[b];
     };
+    auto commit = [&]() { commit_to(BAR_MMA); };
 
     if (tid == 0 && NC > 0) {
         load_q(0);
         load_k(0);
         load_v(0);
     }
-    if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)
+    if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)  // z is consumed by warps 4-7 (gate precompute)
     // Gate inputs of the next chunk are prefetched into warp 0's registers (lane l: tokens 2l,
     // 2l+1) as raw values: loaded unconditionally (positions past the sequence end are clamped
     // to its last token), transformed and masked only when that chunk is processed, so that
@@ -495,6 +497,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 put8_split(sb + OFF_TPP_HI + co, sb + OFF_TPP_LO + co, tpp + 8 * hh, true);
             }
         }
+        wait_bar(BAR_V, ph);
+        if (p.prestage) {  // fp16 v -> bf16 in place (gdnChunkPrefillSm87.cu:88-98); each thread its own words
+#pragma unroll
+            for (int e = tid; e < 1024; e += NTHREADS) {
+                uint32_t w4[4];
+                const uint32_t a = sb + OFF_V + (uint32_t)e * 16;
+                ld_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const __half2 h2 = *reinterpret_cast<const __half2*>(&w4[u]);
+                    w4[u] = pack_bf16(__low2float(h2), __high2float(h2));
+                }
+                st_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
+            }
+        }
         ptx::fence_proxy_async_smem();
         __syncthreads();
 
@@ -508,6 +525,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 ptx::mma_bf16(tmem + TM_W, a, b, ID_W, s > 0);
             }
             commit();
+            // C12's state-free part v^T [T'_hi; T'_lo]^T into the dS columns (dS of the previous
+            // chunk has been read): cols 0-63 the hi terms, 64-127 the lo terms (B stacked along N).
+            // The next commit (after C12's state part) covers it.
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const uint64_t a = desc(dlo8k, OFF_V + s * 2048);
+                const uint64_t b = desc(dlo16, OFF_TP_HI + s * 32);
+                ptx::mma_bf16(tmem + TM_C12, a, b, ID_U, s > 0);
+            }
         }
         wait_mma();
         {   // thread (dk = row, half): W^T[dk][tok] for tok in [32*half, +32), written as rows of W^T
@@ -533,33 +559,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         __syncthreads();
         if (*abort_flag) break;
 
-        // ---- C12: v_new^T = v^T T'^T - S^T W^T ----
-        wait_bar(BAR_V, ph);
-        if (p.prestage) {  // fp16 v -> bf16 in place (gdnChunkPrefillSm87.cu:88-98)
-#pragma unroll
-            for (int e = tid; e < 1024; e += NTHREADS) {
-                uint32_t w4[4];
-                const uint32_t a = sb + OFF_V + (uint32_t)e * 16;
-                ld_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const __half2 h2 = *reinterpret_cast<const __half2*>(&w4[u]);
-                    w4[u] = pack_bf16(__low2float(h2), __high2float(h2));
-                }
-                st_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
-            }
-            ptx::fence_proxy_async_smem();
-            __syncthreads();
-        }
+        // ---- C12: v_new^T = v^T T'^T - S^T W^T (the v^T T'^T part was issued with P3) ----
         if (tid == 0) {
             ptx::tc_fence_after();
-            // cols 0-63 accumulate the hi terms, cols 64-127 the lo terms (B stacked along N)
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const uint64_t a = desc(dlo8k, OFF_V + s * 2048);
-                const uint64_t b = desc(dlo16, OFF_TP_HI + s * 32);  // [T'_hi; T'_lo]
-                ptx::mma_bf16(tmem + TM_V, a, b, ID_U, s > 0);
-            }
             // S_hi [W_hi | W_lo], then S_lo W_hi (N = 64: the S_lo W_lo term is below the precision
             // of the split and is left out); S^T from TMEM, W^T tiles MN-major (LBO = 16 KB)
 #pragma unroll
@@ -568,19 +570,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
                     const uint64_t b = desc(dlo16k, OFF_W_HI + s * 2048);
-                    ptx::mma_bf16_ts(tmem + TM_V, tmem + sa + 8 * s, b, part ? ID_WS_HI : ID_WS, 1u);
+                    ptx::mma_bf16_ts(tmem + TM_C12, tmem + sa + 8 * s, b, part ? ID_WS_HI : ID_WS, 1u);
                 }
             }
             commit();
         }
         wait_mma();
         if (tid == 0 && n + 1 < NC) load_v(n + 1);  // v tile consumed
-        {   // v_new^T (fp32, cols TM_V) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
+        {   // v_new^T (fp32, cols TM_C12) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
             {
                 float v2[32];
-                ptx::tmem_ld32(tl + TM_V + 32 * half, v);
-                ptx::tmem_ld32(tl + TM_V + 64 + 32 * half, v2);
+                ptx::tmem_ld32(tl + TM_C12 + 32 * half, v);
+                ptx::tmem_ld32(tl + TM_C12 + 64 + 32 * half, v2);
                 ptx::tmem_wait_ld();
 #pragma unroll
                 for (int jj = 0; jj < 32; jj += 2)
@@ -604,9 +606,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 f2_unpack(f2_mul(f2_pack(v[2 * j], v[2 * j + 1]), f2_pack(ed_s[32 * half + 2 * j], ed_s[32 * half + 2 * j + 1])), w0, w1);
                 split2x(w0, w1, ph_[j], pl[j]);
             }
-            ptx::tc_fence_before();
-            __syncthreads();  // every thread has read TM_V before cols [64, 192) are reused
-            ptx::tc_fence_after();
             ptx::tmem_st16(tl + TM_VP_HI + 16 * half, ph_);
             ptx::tmem_st16(tl + TM_VP_LO + 16 * half, pl);
             ptx::tmem_wait_st();
@@ -615,9 +614,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         __syncthreads();
         if (*abort_flag) break;
 
-        // ---- C3: o1^T = S^T q^T, o2^T = v_new^T M^T ; C4: dS^T = v_new'^T K ----
+        // ---- C4: dS^T = v_new'^T K ; C3: o1^T = S^T q^T, o2^T = v_new^T M^T. dS first, each group
+        //      with its own commit, so that the state update overlaps the output products ----
         if (tid == 0) {
             ptx::tc_fence_after();
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+                const uint32_t va = part ? TM_VP_LO : TM_VP_HI;
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const uint64_t b = desc(dlo16k, OFF_QK + 8192 + s * 2048);
+                    ptx::mma_bf16_ts(tmem + TM_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
+                }
+            }
+            commit_to(BAR_DS);
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
                 const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
@@ -627,6 +637,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                     ptx::mma_bf16_ts(tmem + TM_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
                 }
             }
+            commit_to(BAR_O1);
             // (VN_hi, M_hi), (VN_lo, M_hi), (VN_hi, M_lo)
 #pragma unroll
             for (int term = 0; term < 3; ++term) {
@@ -638,22 +649,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                     ptx::mma_bf16_ts(tmem + TM_O2, tmem + va + 8 * s, b, ID_O, (term | s) > 0);
                 }
             }
-#pragma unroll
-            for (int part = 0; part < 2; ++part) {
-                const uint32_t va = part ? TM_VP_LO : TM_VP_HI;
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint64_t b = desc(dlo16k, OFF_QK + 8192 + s * 2048);
-                    ptx::mma_bf16_ts(tmem + TM_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
-                }
-            }
             commit();
         }
-        wait_mma();
-        if (tid == 0 && n + 1 < NC) {  // q and k tiles consumed
-            load_q(n + 1);
-            load_k(n + 1);
-        }
+        wait_bar(BAR_DS, consumed[BAR_DS] & 1u);
+        ptx::tc_fence_after();
 
         // ---- state update: S <- e^{cL} S + dS; new S^T hi/lo into TMEM ----
         {
@@ -671,6 +670,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
             }
         }
+        wait_bar(BAR_O1, consumed[BAR_O1] & 1u);  // S^T q^T has read the old state operand and q
+        ptx::tc_fence_after();
+        if (tid == 0 && n + 1 < NC) {  // q and k tiles consumed (k by dS)
+            load_q(n + 1);
+            load_k(n + 1);
+        }
+        store_state_operand();  // new S^T hi/lo for the next chunk's C12 / C3, while v_new^T M^T runs
+        wait_mma();             // v_new^T M^T done
 
         // ---- o = scale e^c o1 + o2, rounded to bf16, staged [tok][dv] in the (free) L region ----
         {
@@ -689,7 +696,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) ot[sw_off(32 * half + jj, dv, 64) >> 1] = __float2bfloat16_rn(v[jj]);
         }
-        store_state_operand();  // new S^T hi/lo for the next chunk's C12 / C3
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncthreads();
@@ -770,7 +776,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     // in flight before its shared memory and TMEM are released.
     if (*abort_flag && (tid == 0 || tid == 128)) {
 #pragma unroll
-        for (int i = 0; i < 5; ++i)
+        for (int i = 0; i < NBAR; ++i)
             while (consumed[i] < issued[i]) {
                 ptx::mbar_wait(bar(i), consumed[i] & 1u, WAIT_ITERS);
                 ++consumed[i];
