@@ -110,6 +110,11 @@ enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4, BAR_DS = 5, BAR_
 constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192,
               DBG_O = DBG_VN + 8192, DBG_SC = DBG_O + 8192, DBG_REC = DBG_SC + 16384;
 
+// The pre-stage (TRT adapter) mode and the debug dumps are template parameters: the
+// instantiation that serves the plain and gated paths carries neither's code in its loop
+// (the kernel is sensitive to instruction fetch; its loop body is larger than an SM's
+// instruction cache).
+template <bool kPrestage, bool kDebug>
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
     // the tensor maps are kernel parameters, not data of the previous launch: fetch them while it ends
     if (threadIdx.x == 0) {
@@ -200,7 +205,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     float* w_s = misc + MISC_W / 4;
     if (tid < HD)
         w_s[tid] = !p.gated ? 0.f
-                   : (p.prestage ? __half2float(reinterpret_cast<const __half*>(p.w)[tid]) : __bfloat162float(p.w[tid]));
+                   : (kPrestage ? __half2float(reinterpret_cast<const __half*>(p.w)[tid]) : __bfloat162float(p.w[tid]));
 
     // ---- TMA issue helpers (thread 0) ----
     uint32_t issued[NBAR] = {0, 0, 0, 0, 0, 0, 0}, consumed[NBAR] = {0, 0, 0, 0, 0, 0, 0};
@@ -268,14 +273,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     __half an0 = __float2half(0.f), an1 = an0, bh0 = an0, bh1 = an0;  // pre-stage a, b
     // Pre-stage gate math (gdnChunkPrefillSm87.cu:44-49, 113-125):
     // g = -exp(A_log[h]) * softplus(a + dt_bias[h]) (threshold 20), beta = sigmoid(b).
-    const float gA = p.prestage ? -expf(__ldg(p.A_log + h)) : 0.f;
-    const float gdt = p.prestage ? __half2float(p.dt_bias[h]) : 0.f;
+    const float gA = kPrestage ? -expf(__ldg(p.A_log + h)) : 0.f;
+    const float gdt = kPrestage ? __half2float(p.dt_bias[h]) : 0.f;
     auto load_gates = [&](int n) {
         const int last = len - n * CS - 1;
         const long long t0 = tok_base + (long long)n * CS;
         const size_t i0 = (size_t)(t0 + min(2 * lane, last)) * p.HV + h;
         const size_t i1 = (size_t)(t0 + min(2 * lane + 1, last)) * p.HV + h;
-        if (p.prestage) {
+        if (kPrestage) {
             an0 = ldg_early(p.ga + i0);
             bh0 = ldg_early(p.gb + i0);
             an1 = ldg_early(p.ga + i1);
@@ -290,7 +295,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     auto gate_of = [&](bool valid, float g_raw, float b_raw, __half a_raw, __half bb_raw, float& gv, float& bv) {
         if (!valid) {
             gv = bv = 0.f;
-        } else if (p.prestage) {
+        } else if (kPrestage) {
             const float x = __half2float(a_raw) + gdt;
             gv = gA * (x > 20.f ? x : log1pf(expf(x)));
             bv = 1.f / (1.f + expf(-__half2float(bb_raw)));
@@ -322,7 +327,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         const int valid = min(CS, len - n * CS);
         const long long tok0 = tok_base + (long long)n * CS;
         const uint32_t ph = (uint32_t)(n & 1);
-        float* rec = p.dbg ? p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC : nullptr;
+        float* rec = (kDebug && p.dbg != nullptr) ? p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC : nullptr;
 
         // ---- gates: in-chunk inclusive cumsum of g (warp scan), decay factors ----
         if (warp == 0) {
@@ -351,7 +356,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         // ---- P1: [Q;K] K^T ----
         wait_bar(BAR_Q, ph);
         wait_bar(BAR_K, ph);
-        if (p.prestage) {
+        if (kPrestage) {
             // fp16 q/k rows -> fp32 L2 normalisation (eps 1e-6 inside the rsqrt) -> bf16, in
             // place; two threads per row (64 elements each), rows 0-63 q, 64-127 k.
             const int r = tid >> 1, hf = tid & 1;
@@ -446,7 +451,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     float z0, z1;
-                    if (p.prestage) {
+                    if (kPrestage) {
                         const __half2 z2 = *reinterpret_cast<const __half2*>(&w4[e]);
                         z0 = __low2float(z2), z1 = __high2float(z2);
                     } else {
@@ -498,7 +503,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             }
         }
         wait_bar(BAR_V, ph);
-        if (p.prestage) {  // fp16 v -> bf16 in place (gdnChunkPrefillSm87.cu:88-98); each thread its own words
+        if (kPrestage) {  // fp16 v -> bf16 in place (gdnChunkPrefillSm87.cu:88-98); each thread its own words
 #pragma unroll
             for (int e = tid; e < 1024; e += NTHREADS) {
                 uint32_t w4[4];
@@ -718,20 +723,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             // Output rounding: bf16, or in pre-stage mode fp16 (o is already a bf16 value,
             // exactly representable in fp16 inside its range, as the adapter's bf16->fp16 bridge).
             auto pack_out = [&](float a, float b) -> uint32_t {
-                if (p.prestage) {
+                if (kPrestage) {
                     const __half2 h2 = __floats2half2_rn(a, b);
                     return *reinterpret_cast<const uint32_t*>(&h2);
                 }
                 return pack_bf16(a, b);
             };
             auto round_in = [&](float x) -> float {  // the norm's round-to-input-dtype step
-                return p.prestage ? __half2float(__float2half_rn(x)) : bf16r(x);
+                return kPrestage ? __half2float(__float2half_rn(x)) : bf16r(x);
             };
             if (!p.gated) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) outw[j] = pack_out(o[2 * j], o[2 * j + 1]);
             } else {
-                if (p.prestage) {  // the norm reads the adapter's fp16 o (bf16 -> fp16 bridge, subnormals included)
+                if (kPrestage) {  // the norm reads the adapter's fp16 o (bf16 -> fp16 bridge, subnormals included)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) o[j] = __half2float(__float2half_rn(o[j]));
                 }
@@ -837,8 +842,11 @@ static cudaError_t ensure_smem_attr() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = (dev < 64) ? (1ull << dev) : 0;
     if (bit && (done_mask.load(std::memory_order_acquire) & bit)) return cudaSuccess;
-    e = cudaFuncSetAttribute(gdn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)SMEM_ALLOC);
+    for (auto fn : {gdn_prefill_kernel<false, false>, gdn_prefill_kernel<true, false>, gdn_prefill_kernel<false, true>,
+                    gdn_prefill_kernel<true, true>}) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_ALLOC);
+        if (e != cudaSuccess) break;
+    }
     if (e == cudaSuccess && bit) done_mask.fetch_or(bit, std::memory_order_acq_rel);
     return e;
 }
@@ -955,7 +963,9 @@ static cudaError_t launch(const Launch& L) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, gdn_prefill_kernel, p);
+    void (*kernel)(Params) = L.prestage ? (L.dbg ? gdn_prefill_kernel<true, true> : gdn_prefill_kernel<true, false>)
+                                        : (L.dbg ? gdn_prefill_kernel<false, true> : gdn_prefill_kernel<false, false>);
+    e = cudaLaunchKernelEx(&cfg, kernel, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
