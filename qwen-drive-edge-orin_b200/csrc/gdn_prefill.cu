@@ -264,8 +264,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         load_k(0);
         load_v(0);
     }
-    if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)  // z is consumed by warps 4-7 (gate precompute)
-    // Gate inputs of the next chunk are prefetched into warp 0's registers (lane l: tokens 2l,
+    if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)
+    // Gate inputs of the next chunk are prefetched into warp 1's registers (lane l: tokens 2l,
     // 2l+1) as raw values: loaded unconditionally (positions past the sequence end are clamped
     // to its last token), transformed and masked only when that chunk is processed, so that
     // nothing waits on these loads earlier.
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             bv = b_raw;
         }
     };
-    if (warp == 0 && NC > 0) load_gates(0);
+    if (warp == 1 && NC > 0) load_gates(0);
     ptx::tmem_wait_st();
     ptx::tc_fence_before();
     __syncthreads();
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         float* rec = (kDebug && p.dbg != nullptr) ? p.dbg + (((size_t)seq * p.HV + h) * p.max_nc + n) * DBG_REC : nullptr;
 
         // ---- gates: in-chunk inclusive cumsum of g (warp scan), decay factors ----
-        if (warp == 0) {
+        if (warp == 1) {  // warp 1: thread 0 (warp 0) issues P1 meanwhile
             float g0, g1, b0, b1;
             gate_of(2 * lane < valid, gn0, bn0, an0, bh0, g0, b0);
             gate_of(2 * lane + 1 < valid, gn1, bn1, an1, bh1, g1, b1);
