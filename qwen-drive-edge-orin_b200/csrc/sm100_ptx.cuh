@@ -43,10 +43,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of a phase (returns at once, completed or not).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: returns false after ~max_iters polls (with backoff). The poll loop is kept
 // rolled: unrolled at each of the many inlined call sites it multiplies the kernel's code
 // size and the instruction-cache misses that come with it.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t max_iters) {
+    if (mbar_test_wait(bar, parity)) return true;  // phase already complete: no suspend window
 #pragma unroll 1
     for (uint32_t it = 0; it < max_iters; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
