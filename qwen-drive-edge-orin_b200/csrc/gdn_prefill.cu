@@ -5,14 +5,18 @@
 // One CTA owns one (sequence, v-head) pair and walks its 64-token chunks in
 // order. Per chunk n (c = in-chunk cumsum of g, L = strict-lower
 // beta_i (k_i.k_j) e^{c_i-c_j}, T = (I+L)^-1):
+//   --  gates: c, e^c, e^{c_L-c} by a warp scan (warp 1, while thread 0 issues P1)
 //   P1  [Q;K] K^T            -> q.k (rows 0-63) and k.k (rows 64-127)  tcgen05, M=128
-//   --  L, M = scale (q k^T) * decay  (registers), T by blocked forward
-//       substitution (CUDA cores, fp32)
-//   P3  W    = (T diag(beta e^c)) K                                  tcgen05, M=64, N=128
-//   C12 v_new^T = v^T (T diag(beta))^T - S^T W^T                    tcgen05, M=128
-//   C3  o^T  = scale e^c (S^T q^T) + v_new^T M^T  (two accumulators)  tcgen05, M=128
+//   --  L, M = scale (q k^T) * decay  (registers); T: diagonal blocks by forward
+//       substitution (CUDA cores), off-diagonal block products as tf32x3 mma.sync
+//   P3  W^T  = K^T (T diag(beta e^c))^T, with C12's state-free part v^T T'^T  tcgen05, M=128
+//   C12 v_new^T = v^T (T diag(beta))^T - S^T W^T  (in the dS columns) tcgen05, M=128
 //   C4  dS^T = (v_new e^{c_L-c})^T K                                 tcgen05, M=128, N=128
-//   --  S <- e^{c_L} S + dS (fp32 registers); o -> gated RMSNorm -> y
+//   C3  o^T  = scale e^c (S^T q^T) + v_new^T M^T  (two accumulators)  tcgen05, M=128
+//   --  S <- e^{c_L} S + dS (fp32 registers) while C3 runs; o -> gated RMSNorm -> y
+// Thread 0 issues every MMA (an issue occupies the thread for about the
+// instruction's execution time); dS, S^T q^T and v_new^T M^T commit to separate
+// barriers so that the state update and the new state operand overlap C3.
 // Transposed forms put the 128-wide feature dimension on the MMA M axis so
 // every accumulator row is one TMEM lane, which makes the state update
 // thread-local; the norm epilogue re-reads o through a swizzled shared tile
