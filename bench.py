@@ -336,7 +336,12 @@ def main():
     achieved_gbs = step_bytes / (ms_step / 1e3) / 1e9
     flops = alg_flops(B, T, HV)
     traffic, traffic_kernel = load_traffic(args.config)
-    roofline = {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
+    override = os.environ.get("GDN_B200_KERNEL", "auto")
+    if override in ("fused", "split"):  # the launcher's kernel choice was overridden
+        launched = "gdn::split::gdn_prefill_split_kernel" if override == "split" else "gdn::gdn_prefill_kernel"
+        if traffic_kernel != launched:  # the committed traffic figure is another kernel's
+            traffic, traffic_kernel = None, launched
+    roofline ={"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
                 "frac": round(achieved_gbs / hbm_gbs, 4), "traffic": traffic,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
                 "alg_bytes_per_launch": step_bytes, "alg_flops_per_launch": flops,
