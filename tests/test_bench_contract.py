@@ -1,0 +1,54 @@
+"""CPU checks of bench.py's roofline arithmetic and its committed inputs.
+
+The bench line's ``roofline.achieved`` is algorithmic bytes per launch divided by the
+kernel's event-timed duration, so the byte and FLOP counts must equal the per-unit figures
+the design states: 33,024 B per token (HQK=16, HV=32, d=128, bf16 q/k/v/z/y, fp32 g/beta)
+plus 2·HV·d²·4 B per sequence for s0 and sf, and 2·(5·C·d + 3·d² + C²/3) FLOP per token
+per v-head (182,954.7 at C=64, d=128).
+"""
+from __future__ import annotations
+
+import json
+
+import pytest
+
+from conftest import ROOT
+
+bench = pytest.importorskip("bench")
+
+
+def test_bytes_per_token_and_per_sequence():
+    per_tok = bench.alg_bytes(1, 1, 16, 32, with_s0=False) - 32 * 128 * 128 * 4
+    assert per_tok == 33_024
+    assert bench.alg_bytes(1, 0, 16, 32) == 2 * 32 * 128 * 128 * 4
+
+
+def test_config1_and_config4_totals():
+    # config 1: 41.87 MB per call; config 4: 4.463 GB per call (one GPU)
+    assert bench.alg_bytes(1, 1141, 16, 32) == 41_874_688
+    assert abs(bench.alg_bytes(32, 4096, 16, 32) / 1e9 - 4.463) < 5e-4
+    assert abs(bench.alg_flops(1, 1141, 32) / 1e9 - 6.680) < 5e-4
+
+
+def test_flops_per_token_per_head():
+    assert abs(bench.alg_flops(1, 1, 1) - 182_954.67) < 0.01
+
+
+def test_configs_match_baseline_shapes():
+    c1, c4 = bench.CONFIGS[1], bench.CONFIGS[4]
+    assert (c1["B"], c1["T"], c1["HQK"], c1["HV"]) == (1, 1141, 16, 32)
+    assert (c4["B"], c4["T"], c4["HQK"], c4["HV"]) == (32, 4096, 16, 32)
+
+
+def test_committed_traffic_and_peaks_are_readable():
+    traffic, kernel = bench.load_traffic(1)
+    assert traffic is not None and kernel == "gdn::split::gdn_prefill_split_kernel"
+    # the kernel reads each input once: DRAM traffic cannot be below the bytes that must come
+    # from HBM (inputs and s0; y and sf may still sit in L2 when the kernel ends)
+    must_read = bench.alg_bytes(1, 1141, 16, 32) - 1141 * 32 * 128 * 2 - 32 * 128 * 128 * 4
+    assert 0.9 * must_read <= traffic <= 1.1 * bench.alg_bytes(1, 1141, 16, 32)
+    hbm, tf_burst, tf_sust, kind = bench.load_peaks()
+    if (ROOT / "MEASURED_PEAKS.json").exists():
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        assert kind == "measured" and hbm == float(d["hbm_gbs"])
+    assert hbm > 1000 and tf_burst > 100
