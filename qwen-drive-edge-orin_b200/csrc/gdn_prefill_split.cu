@@ -466,7 +466,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 // thread takes the same exit decision
                 if (vote_abort()) break;
 
-                wait_bar(B_GREADY + (k & 1), (uint32_t)((k >> 1) & 1));
                 wait_bar(B_Q, ph);
                 wait_bar(B_K, ph);
                 if (tid == 0) {
@@ -481,6 +480,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     commit();
                 }
                 csync();
+                wait_bar(B_GREADY + (k & 1), (uint32_t)((k >> 1) & 1));  // gates (L, M need them; P1 does not)
                 wait_mma(0u);  // P1: the CTA's commits alternate P1 (even phases) and P3 (odd)
                 if (tid == 0 && n + NP < NC) load_q(n + NP);  // P1 has read q
                 {   // rows 0-63: M = scale (q_i k_j) e^{c_i - c_j}, j <= i (hi/lo -> staging);
