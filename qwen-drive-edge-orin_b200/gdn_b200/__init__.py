@@ -21,6 +21,9 @@ from .binding import (  # noqa: F401
     chunk_prefill_debug,
     chunk_prefill_gated,
     chunk_prefill_varlen,
+    chunk_prefill_segmented,
+    segment_bounds,
+    segment_entry_states,
     run_chunk_prefill,
     recurrent_decode,
     gated_rmsnorm,

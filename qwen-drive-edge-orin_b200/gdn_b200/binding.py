@@ -217,6 +217,90 @@ def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, s0=None, z=None, w=None, 
     return [out, sf]
 
 
+# Default number of (segment, v-head) units per pass: the launcher runs up to 74 on the split
+# kernel (two waves of 37 four-CTA clusters on 148 SMs); at config 3's shape 18 segments per
+# sequence (72 units) ran faster than 9 (36 units, one wave): 1.82 vs 2.06 ms, the one-pass call 2.65.
+SEGMENT_UNITS = 74
+
+
+def segment_bounds(B: int, T: int, segments: int):
+    """Cut each of B sequences of T tokens into at most ``segments`` runs of whole chunks.
+
+    Returns (cu_seqlens over the B*T packed tokens as a list of ints, segments per sequence).
+    Every segment but the last of a sequence is a multiple of the chunk length, so the
+    chunking inside a segment is the chunking of the whole sequence.
+    """
+    if B < 1 or T < 1 or segments < 1:
+        raise ValueError("B, T and segments must be positive")
+    nc = (T + CHUNK - 1) // CHUNK
+    per = (nc + min(segments, nc) - 1) // min(segments, nc)  # chunks per segment
+    starts = list(range(0, T, per * CHUNK))
+    cu = []
+    for b in range(B):
+        cu.extend(b * T + t for t in starts)
+    cu.append(B * T)
+    return cu, len(starts)
+
+
+def segment_entry_states(Phi, A, s0=None):
+    """Entry states of consecutive segments: S_0 = s0 (zeros if None), S_{j+1} = Phi_j S_j + A_j.
+
+    Phi, A: [B, nseg, HV, d, d] (segment maps of each sequence, in order); s0: [B, HV, d, d].
+    Returns float32 [B, nseg, HV, d, d]. The scan runs in float64 (a few d x d GEMMs per
+    segment), so its rounding stays below the kernels' and does not depend on TF32 settings.
+    """
+    B, nseg = A.shape[0], A.shape[1]
+    Phi, A = Phi.double(), A.double()
+    S = torch.zeros_like(A[:, 0]) if s0 is None else s0.to(device=A.device, dtype=torch.float64)
+    starts = torch.empty(A.shape, device=A.device, dtype=torch.float32)
+    for j in range(nseg):
+        starts[:, j] = S
+        if j + 1 < nseg:
+            S = torch.matmul(Phi[:, j], S) + A[:, j]
+    return starts
+
+
+def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: float = 1e-6,
+                            segments: int | None = None):
+    """Prefill of long sequences cut into segments that run in parallel: [o or y, final_state].
+
+    Same inputs and results as ``chunk_prefill`` (or ``chunk_prefill_gated`` when z and w are
+    given), for a few long sequences: one 65,536-token stream over 4 v-heads is a 1,024-step
+    chain on 4 clusters of the split kernel, with most of the GPU idle. The state update of a
+    chunk, S <- (e^{cL} I - K^T diag(e^{cL-c}) W) S + K^T diag(e^{cL-c}) U, is affine in S, so a
+    run of chunks maps its entry state as S_end = Phi S_start + A. With each sequence cut at
+    chunk boundaries into segments, three passes of the varlen prefill give the result:
+      1. every segment from a zero state: A (its final state);
+      2. every segment from the identity with v = 0: Phi (U = 0 there, so S_end = Phi I);
+      3. a scan S_{j+1} = Phi_j S_j + A_j (batched 128x128 GEMMs in float64, from s0), then
+         every segment from its S_j, which produces the output and the final state.
+    Each pass runs segments x heads units side by side. ``segments`` defaults to
+    SEGMENT_UNITS / (B * HV) per sequence; with one segment this is the plain call.
+    """
+    B, T, HQK, HV = _check_inputs(q, k, v, g, beta)
+    if (z is None) != (w is None):
+        raise ValueError("pass both z and w (fused norm) or neither")
+    nseg = segments if segments is not None else max(1, SEGMENT_UNITS // (B * HV))
+    cu, per_seq = segment_bounds(B, T, nseg)
+    if per_seq == 1:
+        return chunk_prefill(q, k, v, g, beta, s0) if z is None else chunk_prefill_gated(q, k, v, g, beta, z, w, s0, eps)
+    dev = q.device
+    N = B * per_seq
+    pk = lambda t: t.contiguous().reshape(1, B * T, *t.shape[2:])  # noqa: E731  (packed, B = 1)
+    qp, kp, vp, gp, bp = (pk(t) for t in (q, k, v, g, beta))
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    _, A = chunk_prefill_varlen(qp, kp, vp, gp, bp, cu_t)
+    eye = torch.eye(HEAD_DIM, device=dev, dtype=torch.float32).expand(N, HV, HEAD_DIM, HEAD_DIM).contiguous()
+    _, Phi = chunk_prefill_varlen(qp, kp, torch.zeros_like(vp), gp, bp, cu_t, s0=eye)
+    s0 = None if s0 is None else _state(s0, (B, HV, HEAD_DIM, HEAD_DIM), dev)
+    starts = segment_entry_states(Phi.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM),
+                                  A.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM), s0)
+    zp = None if z is None else pk(z)
+    out, sf = chunk_prefill_varlen(qp, kp, vp, gp, bp, cu_t, s0=starts.view(N, HV, HEAD_DIM, HEAD_DIM), z=zp, w=w,
+                                   eps=eps)
+    return [out.view(B, T, HV, HEAD_DIM), sf.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM)[:, -1].contiguous()]
+
+
 def gated_rmsnorm(o, z, w, eps: float = 1e-6):
     """Standalone gated RMSNorm over the last dim (fp16 or bf16 I/O): the reference's
     ``kernel::gatedRmsNormForward`` (gatedRmsNormKernel.h:16) / ``gated_rmsnorm`` plugin."""
