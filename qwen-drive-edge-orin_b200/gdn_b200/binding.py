@@ -219,7 +219,7 @@ def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, s0=None, z=None, w=None, 
 
 # Default number of (segment, v-head) units per pass: the launcher runs up to 74 on the split
 # kernel (two waves of 37 four-CTA clusters on 148 SMs); at config 3's shape 18 segments per
-# sequence (72 units) ran faster than 9 (36 units, one wave): 1.82 vs 2.06 ms, the one-pass call 2.65.
+# sequence (72 units) ran faster than 9 (36 units, one wave): 1.73 vs 2.02 ms, the one-pass call 2.65.
 SEGMENT_UNITS = 74
 
 
@@ -249,15 +249,17 @@ def segment_entry_states(Phi, A, s0=None):
     Returns float32 [B, nseg, HV, d, d]. The scan runs in float64 (a few d x d GEMMs per
     segment), so its rounding stays below the kernels' and does not depend on TF32 settings.
     """
-    B, nseg = A.shape[0], A.shape[1]
-    Phi, A = Phi.double(), A.double()
-    S = torch.zeros_like(A[:, 0]) if s0 is None else s0.to(device=A.device, dtype=torch.float64)
-    starts = torch.empty(A.shape, device=A.device, dtype=torch.float32)
-    for j in range(nseg):
-        starts[:, j] = S
-        if j + 1 < nseg:
-            S = torch.matmul(Phi[:, j], S) + A[:, j]
-    return starts
+    B, nseg, HV, d = A.shape[0], A.shape[1], A.shape[2], A.shape[3]
+    # [nseg, B*HV, d, d]: one batched GEMM-and-add per step (the scan is launch-bound)
+    Phi = Phi.double().transpose(0, 1).reshape(nseg, B * HV, d, d)
+    A = A.double().transpose(0, 1).reshape(nseg, B * HV, d, d)
+    S = (torch.zeros_like(A[0]) if s0 is None
+         else s0.to(device=A.device, dtype=torch.float64).reshape(B * HV, d, d))
+    states = [S]
+    for j in range(nseg - 1):
+        S = torch.baddbmm(A[j], Phi[j], S)
+        states.append(S)
+    return torch.stack(states, dim=1).view(B, HV, nseg, d, d).transpose(1, 2).float().contiguous()
 
 
 def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: float = 1e-6,
