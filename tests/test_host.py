@@ -95,6 +95,8 @@ def test_binding_rejects_cpu_and_wrong_dtypes():
         gdn_b200.chunk_prefill(q, q, v, g, g)  # CPU tensors
     with pytest.raises(ValueError):
         gdn_b200.binding._check_inputs(q.float(), q, v, g, g)
+    with pytest.raises(ValueError):
+        gdn_b200.chunk_prefill_segmented(q, q, v, g, g, segments=2)  # CPU tensors, before any launch
 
 
 def test_product_path_has_no_oracle_import():
