@@ -282,6 +282,9 @@ def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: floa
     B, T, HQK, HV = _check_inputs(q, k, v, g, beta)
     if (z is None) != (w is None):
         raise ValueError("pass both z and w (fused norm) or neither")
+    if z is not None and (z.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or not z.is_cuda or not w.is_cuda
+                          or tuple(z.shape) != tuple(v.shape) or tuple(w.shape) != (HEAD_DIM,)):
+        raise ValueError("z must be a bf16 CUDA tensor of v's shape and w a bf16 CUDA tensor [128]")
     nseg = segments if segments is not None else max(1, SEGMENT_UNITS // (B * HV))
     cu, per_seq = segment_bounds(B, T, nseg)
     if per_seq == 1:
