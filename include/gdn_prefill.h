@@ -185,6 +185,14 @@ cudaError_t deltanet_chunk_prefill_gated_noalloc(
     int B, int T, int HV, int HQK, int DK, int DV, int chunk_size,
     cudaStream_t stream);
 
+/* No counterpart in the reference. The status word of
+ * deltanet_chunk_prefill_gated_noalloc's static scratch on the current device
+ * (the caller of that entry has no workspace to pass to deltanet_read_status):
+ * copied to *status_host after the work queued on `stream` (synchronises
+ * `stream`); 0 = clean, bit 0 = a bounded wait timed out; cleared when
+ * clear != 0. Allocates nothing. */
+cudaError_t deltanet_noalloc_read_status(int* status_host, int clear, cudaStream_t stream);
+
 /* Copy the device status word of a workspace to *status_host (synchronises
  * `stream`). 0 = clean; bit 0 = a bounded wait timed out. Clears it when
  * clear != 0. No counterpart in the reference (its kernels have no waits). */

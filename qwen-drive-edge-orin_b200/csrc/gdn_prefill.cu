@@ -983,6 +983,7 @@ static cudaError_t launch(const Launch& L) {
 constexpr size_t NOALLOC_SCRATCH_BYTES = 256;  // maximum scratch the no-alloc entry can serve
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 constexpr int NOALLOC_MAX_DEVICES = 64;
+static_assert(WS_HEADER <= NOALLOC_SCRATCH_BYTES, "the static scratch must hold the status header");
 
 static cudaError_t noalloc_scratch(void** out) {
     static std::mutex mu;
@@ -1171,6 +1172,18 @@ cudaError_t deltanet_read_status(void* workspace, int* status_host, int clear, c
     *status_host = (int)s;
     if (clear) e = cudaMemsetAsync(workspace, 0, sizeof(s), stream);
     return e;
+}
+
+// Status word of the no-allocation entry's static scratch on the current device: the same
+// word deltanet_read_status reads from a caller's workspace (0 = clean, bit 0 = a bounded wait
+// timed out), read after the work already queued on `stream` and cleared when clear != 0.
+// Reads only the static array: no allocation here either.
+cudaError_t deltanet_noalloc_read_status(int* status_host, int clear, cudaStream_t stream) {
+    if (!status_host) return cudaErrorInvalidValue;
+    void* ws = nullptr;
+    cudaError_t e = gdn::noalloc_scratch(&ws);
+    if (e != cudaSuccess) return e;
+    return deltanet_read_status(ws, status_host, clear, stream);
 }
 
 const char* gdn_b200_version(void) { return "gdn_b200 0.1 (sm_100a, tcgen05 fused prefill)"; }

@@ -57,9 +57,17 @@ constexpr int NP = 2;                    // prep CTAs per cluster
 // instruction fetch (its hot loops exceed an SM's instruction cache), and it ran faster
 // with the two prep CTAs (the same code) on one pair and the chain and output CTAs on the
 // other than with the chain and a prep CTA paired (config 1: 83.3 -> 80.0 us).
+// Every cross-CTA address (mapa target, slot, barrier) names its CTA by one of these constants;
+// a CTA's own layout (C_*, P_*, U_* offsets and its barriers) is fixed by its role, so a peer's
+// barrier or slot is only valid at the rank that runs that role.
+constexpr uint32_t CHAIN_RANK = 0;       // the chain CTA
 constexpr uint32_t OUT_RANK = 1;         // the output CTA
 constexpr uint32_t PREP_RANK0 = 2;       // prep CTAs: ranks 2 .. NP + 1
 constexpr int CLUSTER = NP + 2;          // chain, NP prep CTAs, output
+static_assert(CHAIN_RANK != OUT_RANK && (CHAIN_RANK < PREP_RANK0 || CHAIN_RANK >= PREP_RANK0 + NP) &&
+                  (OUT_RANK < PREP_RANK0 || OUT_RANK >= PREP_RANK0 + NP) && CHAIN_RANK < CLUSTER &&
+                  OUT_RANK < CLUSTER && PREP_RANK0 + NP <= CLUSTER,
+              "the roles must take distinct ranks of the cluster");
 
 // ---- prep CTA staging layout (one chunk's shipment)
 constexpr uint32_t SL_TP = 0;        // [T'_hi; T'_lo] 128 rows x 64 cols bf16 (K-major, stacked along N)
@@ -157,7 +165,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     const int quarter = warp & 3, half = (warp >> 2) & 1;  // TMEM lane quarter / column half (warps 0-7)
     const int row = quarter * 32 + lane;
     const uint32_t rank = ptx::cluster_ctarank();
-    const bool chain = (rank == 0);
+    const bool chain = (rank == CHAIN_RANK);
     const bool outcta = (rank == OUT_RANK);
     const int h = blockIdx.y;
     const int seq = blockIdx.z;
@@ -585,11 +593,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     auto wait_empty = [&](int b) {
                         if (!ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) fail();
                     };
-                    // the chain CTA's slots and barriers sit at its own offsets
-                    const uint32_t fa = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLA + pi), 0);
-                    const uint32_t fbb = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLB + pi), 0);
-                    const uint32_t da = ptx::mapa(sb + C_ASLOT + (uint32_t)pi * ASLOT, 0);
-                    const uint32_t db = ptx::mapa(sb + C_BSLOT + (uint32_t)pi * B_BYTES, 0);
+                    // the chain CTA's slots and barriers sit at its own offsets, in CTA CHAIN_RANK
+                    const uint32_t fa = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLA + pi), CHAIN_RANK);
+                    const uint32_t fbb = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLB + pi), CHAIN_RANK);
+                    const uint32_t da = ptx::mapa(sb + C_ASLOT + (uint32_t)pi * ASLOT, CHAIN_RANK);
+                    const uint32_t db = ptx::mapa(sb + C_BSLOT + (uint32_t)pi * B_BYTES, CHAIN_RANK);
                     if (k >= 1) wait_empty(B_EMPTYA);
                     ptx::bulk_copy_s2cluster(da + A_TP, sb + stg + SL_TP, SL_M - SL_TP, fa);
                     ptx::bulk_copy_s2cluster(da + A_EC, sb + stg + SL_EC, 512, fa);
@@ -646,7 +654,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         ptx::mbar_arrive_expect_tx(bar(B_FULLO + (n & 1)), O_BYTES);
                     }
                     // the chain CTA's barriers sit at its own misc offset
-                    ptx::mbar_arrive_remote(ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_EMPTYO + (n & 1)), 0));
+                    ptx::mbar_arrive_remote(ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_EMPTYO + (n & 1)), CHAIN_RANK));
                 }
                 float o[32];
 #pragma unroll

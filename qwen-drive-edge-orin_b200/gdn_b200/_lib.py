@@ -35,6 +35,7 @@ SIGNATURES = {
     "deltanet_recurrent_decode": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p] + [c_int] * 6 + [c_void_p]),
     "gated_rmsnorm_forward": (c_int, [c_void_p] * 4 + [c_int64, c_int, c_float, c_int, c_void_p]),
     "deltanet_read_status": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
+    "deltanet_noalloc_read_status": (c_int, [ctypes.POINTER(c_int), c_int, c_void_p]),
     "gdn_b200_version": (ctypes.c_char_p, []),
 }
 

@@ -43,6 +43,15 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
+def _same_device(*ts):
+    """Every given tensor on one CUDA device; returns that device."""
+    ts = [t for t in ts if t is not None]
+    dev = ts[0].device
+    if any(t.device != dev for t in ts):
+        raise ValueError("all tensors must be on the same CUDA device")
+    return dev
+
+
 _ws_lock = threading.Lock()
 _ws_cache: dict = {}
 
@@ -70,13 +79,15 @@ def read_status(device=None, clear: bool = True) -> int:
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
     ws = _workspace(dev, 256)
     out = ctypes.c_int(0)
-    _check(lib.deltanet_read_status(_ptr(ws), ctypes.byref(out), int(clear), _stream()), "deltanet_read_status")
+    with torch.cuda.device(dev):
+        _check(lib.deltanet_read_status(_ptr(ws), ctypes.byref(out), int(clear), _stream()), "deltanet_read_status")
     return out.value
 
 
 def _check_inputs(q, k, v, g, beta, varlen=False):
     if not all(t.is_cuda for t in (q, k, v, g, beta)):
         raise ValueError("all inputs must be CUDA tensors")
+    _same_device(q, k, v, g, beta)
     if not (q.dtype == k.dtype == v.dtype == torch.bfloat16):
         raise ValueError("q/k/v must be bf16")
     if g.dtype != torch.float32 or beta.dtype != torch.float32:
@@ -119,9 +130,10 @@ def _run_prefill(q, k, v, g, beta, s0, debug: bool):
     else:
         nbytes = workspace_size(B, T, HV)
         ws = _workspace(dev, nbytes)
-    code = lib.deltanet_chunk_prefill(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(o), _ptr(s0),
-                                      _ptr(sf), B, T, HV, HQK, HEAD_DIM, HEAD_DIM, CHUNK, _ptr(ws),
-                                      ws.numel(), _stream(), int(debug))
+    with torch.cuda.device(dev):
+        code = lib.deltanet_chunk_prefill(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(o), _ptr(s0),
+                                          _ptr(sf), B, T, HV, HQK, HEAD_DIM, HEAD_DIM, CHUNK, _ptr(ws),
+                                          ws.numel(), _stream(), int(debug))
     _check(code, "deltanet_chunk_prefill")
     if not debug:
         return [o, sf]
@@ -171,6 +183,7 @@ def chunk_prefill_gated(q, k, v, g, beta, z, w, s0=None, eps: float = 1e-6):
         raise ValueError("z and w must be bf16 CUDA tensors")
     if tuple(z.shape) != tuple(v.shape) or tuple(w.shape) != (HEAD_DIM,):
         raise ValueError("z must match v's shape and w must be [128]")
+    _same_device(q, z, w)
     lib = load_library()
     q, k, v, g, beta, z, w = (t.contiguous() for t in (q, k, v, g, beta, z, w))
     dev = q.device
@@ -178,9 +191,10 @@ def chunk_prefill_gated(q, k, v, g, beta, z, w, s0=None, eps: float = 1e-6):
     sf = torch.empty(B, HV, HEAD_DIM, HEAD_DIM, device=dev, dtype=torch.float32)
     s0 = _state(s0, (B, HV, HEAD_DIM, HEAD_DIM), dev)
     ws = _workspace(dev, workspace_size(B, T, HV))
-    code = lib.deltanet_chunk_prefill_gated(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w),
-                                            float(eps), _ptr(y), _ptr(s0), _ptr(sf), B, T, HV, HQK, HEAD_DIM,
-                                            HEAD_DIM, CHUNK, _ptr(ws), ws.numel(), _stream())
+    with torch.cuda.device(dev):
+        code = lib.deltanet_chunk_prefill_gated(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w),
+                                                float(eps), _ptr(y), _ptr(s0), _ptr(sf), B, T, HV, HQK, HEAD_DIM,
+                                                HEAD_DIM, CHUNK, _ptr(ws), ws.numel(), _stream())
     _check(code, "deltanet_chunk_prefill_gated")
     return [y, sf]
 
@@ -196,6 +210,7 @@ def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, s0=None, z=None, w=None, 
     if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1 or not cu_seqlens.is_cuda:
         raise ValueError("cu_seqlens must be a 1-D int32 CUDA tensor")
     N = cu_seqlens.numel() - 1
+    _same_device(q, cu_seqlens, z, w)
     if (z is None) != (w is None):
         raise ValueError("pass both z and w (fused norm) or neither")
     lib = load_library()
@@ -210,9 +225,10 @@ def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, s0=None, z=None, w=None, 
     sf = torch.empty(N, HV, HEAD_DIM, HEAD_DIM, device=dev, dtype=torch.float32)
     s0 = _state(s0, (N, HV, HEAD_DIM, HEAD_DIM), dev)
     ws = _workspace(dev, workspace_size(1, T, HV))
-    code = lib.deltanet_chunk_prefill_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w),
-                                             float(eps), _ptr(out), _ptr(s0), _ptr(sf), _ptr(cu), N, T, HV, HQK,
-                                             HEAD_DIM, HEAD_DIM, CHUNK, _ptr(ws), ws.numel(), _stream())
+    with torch.cuda.device(dev):
+        code = lib.deltanet_chunk_prefill_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w),
+                                                 float(eps), _ptr(out), _ptr(s0), _ptr(sf), _ptr(cu), N, T, HV, HQK,
+                                                 HEAD_DIM, HEAD_DIM, CHUNK, _ptr(ws), ws.numel(), _stream())
     _check(code, "deltanet_chunk_prefill_varlen")
     return [out, sf]
 
@@ -315,13 +331,15 @@ def gated_rmsnorm(o, z, w, eps: float = 1e-6):
         raise ValueError("z must match o and w must be [dv]")
     if not (o.is_cuda and z.is_cuda and w.is_cuda):
         raise ValueError("all inputs must be CUDA tensors")
+    dev = _same_device(o, z, w)
     lib = load_library()
     o, z, w = o.contiguous(), z.contiguous(), w.contiguous()
     y = torch.empty_like(o)
     dv = o.shape[-1]
     rows = o.numel() // dv if dv else 0
-    code = lib.gated_rmsnorm_forward(_ptr(o), _ptr(z), _ptr(w), _ptr(y), rows, dv, float(eps),
-                                     0 if o.dtype == torch.float16 else 1, _stream())
+    with torch.cuda.device(dev):
+        code = lib.gated_rmsnorm_forward(_ptr(o), _ptr(z), _ptr(w), _ptr(y), rows, dv, float(eps),
+                                         0 if o.dtype == torch.float16 else 1, _stream())
     _check(code, "gated_rmsnorm_forward")
     return y
 
@@ -337,6 +355,7 @@ def run_chunk_prefill(q, k, v, a, b, A_log, dt_bias, h0, z=None, norm_w=None, ep
     if A_log.dtype != torch.float32 or h0.dtype != torch.float32 or not h0.is_contiguous():
         raise ValueError("A_log must be fp32 and h0 a contiguous fp32 tensor")
     from ._lib import GdnPrefillParams
+    _same_device(q, k, v, a, b, A_log, dt_bias, h0, z, norm_w)
     lib = load_library()
     n, T, h, kd = q.shape
     hv, vd = v.shape[2], v.shape[3]
@@ -350,7 +369,9 @@ def run_chunk_prefill(q, k, v, a, b, A_log, dt_bias, h0, z=None, norm_w=None, ep
                            o=o.data_ptr(), z=None if z is None else z.data_ptr(),
                            norm_w=None if norm_w is None else norm_w.data_ptr(), eps=float(eps), n=n, seq_len=T, h=h,
                            hv=hv, k_dim=kd, v_dim=vd, workspace=ws.data_ptr(), workspace_bytes=ws.numel())
-    if lib.gdn_run_chunk_prefill(ctypes.byref(prm), _stream()) != 0:
+    with torch.cuda.device(q.device):
+        rc = lib.gdn_run_chunk_prefill(ctypes.byref(prm), _stream())
+    if rc != 0:
         raise GdnError("gdn_run_chunk_prefill failed (see stderr)")
     return o
 
@@ -364,13 +385,15 @@ def recurrent_decode(q, k, v, g, beta, state, z=None, w=None, eps: float = 1e-6)
         raise ValueError("state must be a contiguous fp32 [B, HV, 128, 128] tensor")
     if (z is None) != (w is None):
         raise ValueError("pass both z and w (fused norm) or neither")
+    dev = _same_device(q, state, z, w)
     lib = load_library()
     q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
     if z is not None:
         z, w = z.contiguous(), w.contiguous()
     out = torch.empty_like(v)
-    code = lib.deltanet_recurrent_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w), float(eps),
-                                         _ptr(out), _ptr(state), B, T, HV, HQK, HEAD_DIM, HEAD_DIM, _stream())
+    with torch.cuda.device(dev):
+        code = lib.deltanet_recurrent_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w), float(eps),
+                                             _ptr(out), _ptr(state), B, T, HV, HQK, HEAD_DIM, HEAD_DIM, _stream())
     _check(code, "deltanet_recurrent_decode")
     return out
 

@@ -39,7 +39,9 @@ from transformers.models.qwen3_5.modeling_qwen3_5 import (  # noqa: E402
     torch_recurrent_gated_delta_rule,
 )
 
-REF_HARNESS = Path(os.environ.get("GDN_REFERENCE_ROOT", "/root/reference")) / "kernels/harness/parity_test.py"
+# the reference checkout: $GDN_REFERENCE_ROOT, else a `reference` directory beside this repository
+REF_ROOT = Path(os.environ.get("GDN_REFERENCE_ROOT") or Path(__file__).resolve().parents[3] / "reference")
+REF_HARNESS = REF_ROOT / "kernels/harness/parity_test.py"
 
 
 def verbatim_ref_chunk():

@@ -71,6 +71,33 @@ def test_noalloc_matches_workspace_entry_twice(B, T, HQK, HV):
         print(f"call {call}: identical={np.array_equal(yh, y_ref_h) and np.array_equal(sfh, sf_ref_h)}")
 
 
+def test_noalloc_status_word_is_readable():
+    """A caller of the no-allocation entry has no workspace to hand to deltanet_read_status,
+    so deltanet_noalloc_read_status reads the status word of the library's static scratch:
+    clean (0) after a normal call, and still 0 after being read with clear set."""
+    lib = gdn_b200.load_library()
+    B, T, HQK, HV = 1, 300, 2, 4
+    inp = make_inputs(B, T, HQK, HV, 128, seed=5, dist="baseline", with_s0=True)
+    q, k, v, z, w = (_dev(a) for a in (inp.q, inp.k, inp.v, inp.z, inp.w))
+    g, beta, s0 = (_dev(a, torch.float32) for a in (inp.g, inp.beta, inp.s0))
+    y = torch.empty_like(v)
+    sf = torch.empty(B, HV, 128, 128, device="cuda")
+    vp = ctypes.c_void_p
+    stream = vp(torch.cuda.current_stream().cuda_stream)
+    rc = lib.deltanet_chunk_prefill_gated_noalloc(vp(q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()),
+                                                  vp(g.data_ptr()), vp(beta.data_ptr()), vp(z.data_ptr()),
+                                                  vp(w.data_ptr()), 1e-6, vp(y.data_ptr()), vp(s0.data_ptr()),
+                                                  vp(sf.data_ptr()), B, T, HV, HQK, 128, 128, 64, stream)
+    assert rc == 0
+    st = ctypes.c_int(-1)
+    assert lib.deltanet_noalloc_read_status(ctypes.byref(st), 1, stream) == 0
+    assert st.value == 0
+    st.value = -1
+    assert lib.deltanet_noalloc_read_status(ctypes.byref(st), 0, stream) == 0
+    assert st.value == 0
+    assert lib.deltanet_noalloc_read_status(None, 0, stream) == 1  # cudaErrorInvalidValue
+
+
 def test_noalloc_rejects_bad_arguments():
     lib = gdn_b200.load_library()
     p = ctypes.c_void_p(1 << 20)
