@@ -198,6 +198,27 @@ cudaError_t deltanet_noalloc_read_status(int* status_host, int clear, cudaStream
  * clear != 0. No counterpart in the reference (its kernels have no waits). */
 cudaError_t deltanet_read_status(void* workspace, int* status_host, int clear, cudaStream_t stream);
 
+/* Test hook for failure detection; no counterpart in the reference (its
+ * kernels have no waits; its error convention is the return code,
+ * kernels/chunk_delta_cuda.cu:706-727). Runs deltanet_chunk_prefill_gated with
+ * the v-tile load of chunk `withheld_chunk` never issued, so that the kernel's
+ * bounded wait for that tile runs out (~0.3 s): the kernel sets bit 0 of the
+ * workspace status word, stops its loop, waits (bounded) for the copies and
+ * MMAs it has in flight, frees its tensor memory and returns; y and
+ * final_state are then undefined. kernel: 0 = the launcher's choice, 1 = one
+ * CTA per (sequence, v-head), 2 = the cluster-split kernel
+ * (cudaErrorNotSupported if it cannot run). Returns the launch status. */
+cudaError_t deltanet_test_withheld_load(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    const void* z, const void* norm_w, float eps,
+    void* y,
+    const float* initial_state,
+    float* final_state,
+    int B, int T, int HV, int HQK, int DK, int DV, int chunk_size,
+    void* workspace, size_t workspace_bytes,
+    cudaStream_t stream, int kernel, int withheld_chunk);
+
 /* Library build identifier (for logs and tests). */
 const char* gdn_b200_version(void);
 

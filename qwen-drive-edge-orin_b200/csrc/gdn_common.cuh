@@ -44,6 +44,10 @@ struct Params {
     const __half* gb;
     const float* A_log;
     const __half* dt_bias;
+    // Test hook: the v-tile load of this chunk is never issued (-1: every load is issued), so
+    // that the bounded wait for it runs out and the abort path runs. Set only by
+    // deltanet_test_withheld_load.
+    int withhold_v_chunk;
 };
 
 // Byte offset of bf16 element (row, col) in a 128B-swizzled tile whose panels

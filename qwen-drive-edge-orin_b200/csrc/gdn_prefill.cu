@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     if (tid == 0 && NC > 0) {
         load_q(0);
         load_k(0);
-        load_v(0);
+        if (p.withhold_v_chunk != 0) load_v(0);
     }
     if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)
     // Gate inputs of the next chunk are prefetched into warp 1's registers (lane l: tokens 2l,
@@ -585,7 +585,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             commit();
         }
         wait_mma();
-        if (tid == 0 && n + 1 < NC) load_v(n + 1);  // v tile consumed
+        if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk) load_v(n + 1);  // v tile consumed
         {   // v_new^T (fp32, cols TM_C12) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
             {
@@ -871,7 +871,9 @@ bool split_available();
 // use the one-CTA kernel). A forced split launch fails with cudaErrorNotSupported
 // when the compiled split kernel does not have the register count its register
 // split is written for.
-static bool use_split(int nseq, int HV) {
+static bool use_split(int nseq, int HV, int force) {
+    if (force == 1) return false;
+    if (force == 2) return split_available();
     const char* env = getenv("GDN_B200_KERNEL");
     if (env && strcmp(env, "fused") == 0) return false;
     if (env && strcmp(env, "split") == 0) return true;
@@ -901,7 +903,19 @@ struct Launch {
     int prestage;
     const void *ga, *gb, *dt_bias;
     const float* A_log;
+    // test hook (deltanet_test_withheld_load): kernel choice (0 automatic, 1 one CTA per head,
+    // 2 cluster split) and the chunk whose v-tile load is withheld (-1 none)
+    int force_kernel;
+    int withhold_v_chunk;
 };
+
+// A Launch with every field cleared and no test hook armed.
+static Launch blank_launch() {
+    Launch L;
+    memset(&L, 0, sizeof(L));
+    L.withhold_v_chunk = -1;
+    return L;
+}
 
 static cudaError_t launch(const Launch& L) {
     if (L.DK != HD || L.DV != HD || L.chunk != CS) return cudaErrorInvalidValue;
@@ -951,8 +965,11 @@ static cudaError_t launch(const Launch& L) {
     p.gb = static_cast<const __half*>(L.gb);
     p.A_log = L.A_log;
     p.dt_bias = static_cast<const __half*>(L.dt_bias);
+    p.withhold_v_chunk = L.withhold_v_chunk;
 
-    if (!L.dbg && !L.prestage && use_split(L.nseq, L.HV)) return launch_split(p, L.nseq, L.HV, L.stream);
+    const bool split = !L.dbg && !L.prestage && use_split(L.nseq, L.HV, L.force_kernel);
+    if (L.force_kernel == 2 && !split) return cudaErrorNotSupported;
+    if (split) return launch_split(p, L.nseq, L.HV, L.stream);
     cudaError_t e = ensure_smem_attr();
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg;
@@ -1030,8 +1047,7 @@ cudaError_t deltanet_chunk_prefill(const void* q, const void* k, const void* v, 
                                    float* final_state, int B, int T, int HV, int HQK, int DK, int DV,
                                    int chunk_size, void* workspace, size_t workspace_bytes,
                                    cudaStream_t stream, int dump_debug) {
-    gdn::Launch L;
-    memset(&L, 0, sizeof(L));
+    gdn::Launch L = gdn::blank_launch();
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.out = o;
     L.s0 = initial_state; L.sf = final_state;
     L.nseq = B; L.B = B; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
@@ -1065,8 +1081,7 @@ cudaError_t deltanet_chunk_prefill_gated(const void* q, const void* k, const voi
                                          int DV, int chunk_size, void* workspace,
                                          size_t workspace_bytes, cudaStream_t stream) {
     if (!z || !norm_w) return cudaErrorInvalidValue;
-    gdn::Launch L;
-    memset(&L, 0, sizeof(L));
+    gdn::Launch L = gdn::blank_launch();
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.z = z; L.w = norm_w; L.eps = eps; L.out = y;
     L.s0 = initial_state; L.sf = final_state;
     L.nseq = B; L.B = B; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
@@ -1084,8 +1099,7 @@ cudaError_t deltanet_chunk_prefill_varlen(const void* q, const void* k, const vo
                                           cudaStream_t stream) {
     if (!cu_seqlens || N < 0) return cudaErrorInvalidValue;
     if ((z == nullptr) != (norm_w == nullptr)) return cudaErrorInvalidValue;
-    gdn::Launch L;
-    memset(&L, 0, sizeof(L));
+    gdn::Launch L = gdn::blank_launch();
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.z = z; L.w = norm_w; L.eps = eps; L.out = out;
     L.s0 = initial_states; L.sf = final_states; L.cu = cu_seqlens;
     L.nseq = N; L.B = 1; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
@@ -1119,6 +1133,27 @@ cudaError_t deltanet_chunk_prefill_gated_noalloc(const void* q, const void* k, c
                                         HV, HQK, DK, DV, chunk_size, ws, gdn::NOALLOC_SCRATCH_BYTES, stream);
 }
 
+// Test hook for the bounded waits: the gated prefill with one v-tile load never issued, so that
+// the wait for it runs out (the form of failure the kernels must survive: a producer that never
+// arrives). No fault, trap or unbounded wait is involved.
+cudaError_t deltanet_test_withheld_load(const void* q, const void* k, const void* v, const float* g,
+                                        const float* beta, const void* z, const void* norm_w, float eps,
+                                        void* y, const float* initial_state, float* final_state, int B, int T,
+                                        int HV, int HQK, int DK, int DV, int chunk_size, void* workspace,
+                                        size_t workspace_bytes, cudaStream_t stream, int kernel,
+                                        int withheld_chunk) {
+    if (!z || !norm_w || kernel < 0 || kernel > 2 || withheld_chunk < 0) return cudaErrorInvalidValue;
+    gdn::Launch L = gdn::blank_launch();
+    L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.z = z; L.w = norm_w; L.eps = eps; L.out = y;
+    L.s0 = initial_state; L.sf = final_state;
+    L.nseq = B; L.B = B; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
+    L.max_nc = (T + gdn::CS - 1) / gdn::CS;
+    L.ws = workspace; L.ws_bytes = workspace_bytes; L.stream = stream;
+    L.force_kernel = kernel;
+    L.withhold_v_chunk = withheld_chunk;
+    return gdn::launch(L);
+}
+
 int gdn_run_chunk_prefill(const gdn_prefill_params* params, cudaStream_t stream) {
     if (params == nullptr) {
         fprintf(stderr, "gdn_run_chunk_prefill: null params\n");
@@ -1146,8 +1181,7 @@ int gdn_run_chunk_prefill(const gdn_prefill_params* params, cudaStream_t stream)
         fprintf(stderr, "gdn_run_chunk_prefill: pass both z and norm_w to fuse the norm, or neither\n");
         return -1;
     }
-    gdn::Launch L;
-    memset(&L, 0, sizeof(L));
+    gdn::Launch L = gdn::blank_launch();
     L.q = P.q; L.k = P.k; L.v = P.v; L.z = P.z; L.w = P.norm_w; L.eps = P.eps; L.out = P.o;
     L.s0 = P.h0_source; L.sf = P.h0_source;  // initial state in, final state out, in place
     L.nseq = P.n; L.B = P.n; L.T = P.seq_len; L.HV = P.hv; L.HQK = P.h; L.DK = P.k_dim; L.DV = P.v_dim;

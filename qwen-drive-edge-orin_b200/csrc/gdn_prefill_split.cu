@@ -329,12 +329,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             //      o^T [128 dv][64 tok] with 128-byte rows in 16-byte chunks XOR-swizzled by (dv & 7):
             //      one thread writes its row half with four 16-byte stores. Runs at the top of chunk
             //      m + 1's iteration, under the wait for C12(m + 1), so that it is off the recurrence.
-            auto stage_output = [&](int m) {
+            // Returns false when the wait for the output CTA's hand-back of the buffer ran out: the
+            // buffer's slot in the output CTA is then not armed, and o(m) must not be shipped.
+            auto stage_output = [&](int m) -> bool {
                 wait_bar(B_Y, (uint32_t)(m & 1));
                 ptx::tc_fence_after();
                 // the output CTA has handed back this buffer (its chunk m - 2)
-                if (m >= 2 && !ptx::mbar_wait(bar(B_EMPTYO + (m & 1)), (uint32_t)(((m >> 1) - 1) & 1), WAIT_ITERS))
+                bool handed_back = true;
+                if (m >= 2 && !ptx::mbar_wait(bar(B_EMPTYO + (m & 1)), (uint32_t)(((m >> 1) - 1) & 1), WAIT_ITERS)) {
                     fail();
+                    handed_back = false;
+                }
                 const float* ecm = ecl + (m & 1) * CS;
                 const uint32_t ob = sb + C_OST + (uint32_t)(m & 1) * O_BYTES;
 #pragma unroll
@@ -353,10 +358,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                                      pack_bf16(v[8 * c + 6], v[8 * c + 7]));
                 }
                 ptx::fence_proxy_async_smem();  // the staging buffer is read by a bulk copy
+                return handed_back;
             };
-            // after a barrier of warps 0-7 that follows stage_output(m): thread 0 ships o(m)
-            auto ship_output = [&](int m) {
-                if (tid == 0) {
+            // after a barrier of warps 0-7 that follows stage_output(m): thread 0 ships o(m) if its own
+            // wait for the buffer's hand-back succeeded (a copy into an unarmed slot of the output CTA
+            // could still be in flight when the cluster exits)
+            auto ship_output = [&](int m, bool handed_back) {
+                if (tid == 0 && handed_back) {
                     const uint32_t dst = ptx::mapa(sb + U_OSLOT + (uint32_t)(m & 1) * O_BYTES, OUT_RANK);
                     const uint32_t fb = ptx::mapa(sb + U_MISC + M_BAR + 8u * (uint32_t)(B_FULLO + (m & 1)), OUT_RANK);
                     ptx::bulk_copy_s2cluster(dst, sb + C_OST + (uint32_t)(m & 1) * O_BYTES, O_BYTES, fb);
@@ -366,11 +374,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 if (vote_abort()) break;
                 const uint32_t ph = (uint32_t)(n & 1);
                 const float* ecn = ecl + (n & 1) * CS;
-                if (n > 0) stage_output(n - 1);
+                const bool o_ok = (n > 0) ? stage_output(n - 1) : false;
                 if (n == NC) {
                     if (n > 0) {
                         csync();
-                        ship_output(n - 1);
+                        ship_output(n - 1, o_ok);
                     }
                     break;
                 }
@@ -419,7 +427,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     hand_off(B_VNR);
                 }
                 csync();  // e^c copied for every thread; o(n - 1) staged
-                if (n > 0) ship_output(n - 1);
+                if (n > 0) ship_output(n - 1, o_ok);
 
                 // ---- S <- e^{cL} S + dS; the new S^T hi/lo operand (S^T q^T has read the old one)
                 wait_bar(B_X1, ph);
@@ -590,19 +598,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 ptx::fence_proxy_async_smem();
                 csync();
                 if (tid == 0) {  // ship each part once the chain has handed back that part of the previous chunk
+                    // A part is shipped only if its hand-back arrived: after a wait that ran out, the chain's
+                    // slot is not armed, and the copy could still be in flight when the cluster exits.
                     auto wait_empty = [&](int b) {
-                        if (!ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) fail();
+                        if (ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) return true;
+                        fail();
+                        return false;
                     };
                     // the chain CTA's slots and barriers sit at its own offsets, in CTA CHAIN_RANK
                     const uint32_t fa = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLA + pi), CHAIN_RANK);
                     const uint32_t fbb = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLB + pi), CHAIN_RANK);
                     const uint32_t da = ptx::mapa(sb + C_ASLOT + (uint32_t)pi * ASLOT, CHAIN_RANK);
                     const uint32_t db = ptx::mapa(sb + C_BSLOT + (uint32_t)pi * B_BYTES, CHAIN_RANK);
-                    if (k >= 1) wait_empty(B_EMPTYA);
-                    ptx::bulk_copy_s2cluster(da + A_TP, sb + stg + SL_TP, SL_M - SL_TP, fa);
-                    ptx::bulk_copy_s2cluster(da + A_EC, sb + stg + SL_EC, 512, fa);
-                    if (k >= 1) wait_empty(B_EMPTYB);
-                    ptx::bulk_copy_s2cluster(db, sb + stg + SL_M, B_BYTES, fbb);
+                    if (k == 0 || wait_empty(B_EMPTYA)) {
+                        ptx::bulk_copy_s2cluster(da + A_TP, sb + stg + SL_TP, SL_M - SL_TP, fa);
+                        ptx::bulk_copy_s2cluster(da + A_EC, sb + stg + SL_EC, 512, fa);
+                    }
+                    if (k == 0 || wait_empty(B_EMPTYB)) ptx::bulk_copy_s2cluster(db, sb + stg + SL_M, B_BYTES, fbb);
                 }
             }
             if (tid == 0 && k >= 1 && !*abort_flag) {  // the last shipment must land before this CTA exits
@@ -861,12 +873,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             if (lane == 0 && NC > 0) {
                 load_q(0);
                 load_k(0);
-                load_v(0);
+                if (p.withhold_v_chunk != 0) load_v(0);
                 for (int n = 0; n < NC; ++n) {
                     if (*abort_flag) break;
                     const uint32_t ph = (uint32_t)(n & 1);
                     wait_bar(B_VT, ph);  // v^T T'^T has read the v tile
-                    if (n + 1 < NC) load_v(n + 1);
+                    if (n + 1 < NC && n + 1 != p.withhold_v_chunk) load_v(n + 1);
                     prefetch_tile(&p.tm_v, h, n + 2);
                     wait_bar(B_VNR, ph);  // C12 read part A; decay factors copied
                     if (n + NSLOT < NC) arm_slot(B_FULLA, n, A_BYTES);

@@ -31,6 +31,8 @@ SIGNATURES = {
                                       + [c_void_p, c_size_t, c_void_p]),
     "deltanet_chunk_prefill_gated_noalloc": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p, c_void_p]
                                              + [c_int] * 7 + [c_void_p]),
+    "deltanet_test_withheld_load": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p, c_void_p]
+                                    + [c_int] * 7 + [c_void_p, c_size_t, c_void_p, c_int, c_int]),
     "gdn_run_chunk_prefill": (c_int, [c_void_p, c_void_p]),
     "deltanet_recurrent_decode": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p] + [c_int] * 6 + [c_void_p]),
     "gated_rmsnorm_forward": (c_int, [c_void_p] * 4 + [c_int64, c_int, c_float, c_int, c_void_p]),

@@ -52,6 +52,28 @@ def test_segmented_matches_plain(B, T, HQK, HV, segments, gated):
     assert tensor_l2_rel(sf, sf_ref) < 1e-4
 
 
+def test_segmented_slow_decay_against_oracle():
+    """Slow-decay heads (g = -U(0, 0.002), beta = U(0, 0.3)) with random initial states: each
+    segment's state map Phi is far from zero, so the entry states come from the scan rather than
+    being forgotten. Five segments of a 4,133-token sequence against the serial oracle and the
+    one-pass call (with fast decay Phi underflows and the scan is not exercised)."""
+    import dataclasses
+
+    from oracle import gdn_oracle as O
+    base = make_inputs(1, 4133, 2, 4, seed=13, with_s0=True)
+    rng = np.random.default_rng(13)
+    inp = dataclasses.replace(base, g=-(rng.random(base.g.shape) * 0.002).astype(np.float32),
+                              beta=(rng.random(base.beta.shape) * 0.3).astype(np.float32))
+    o_ref, sf_ref = O.chunk_gated_delta_rule(inp.q, inp.k, inp.v, inp.g, inp.beta, 64, inp.s0)
+    o_one, sf_one = _run("plain", inp, False)
+    o, sf = _run("segmented", inp, False, segments=5)
+    print({"o_abs_oracle": max_abs(o, o_ref), "st_rel_oracle": tensor_l2_rel(sf, sf_ref),
+           "o_abs_onepass": max_abs(o, o_one), "st_rel_onepass": tensor_l2_rel(sf, sf_one)})
+    assert max_abs(o, o_ref) <= O_MAX_ABS and tensor_l2_rel(sf, sf_ref) <= 1e-2
+    assert max_rel(sf, sf_ref) < 1e-2
+    assert max_abs(o, o_one) <= O_MAX_ABS / 4 and tensor_l2_rel(sf, sf_one) < 1e-4
+
+
 def test_one_segment_is_the_plain_call():
     inp = make_inputs(1, 700, 2, 4, seed=12)
     o_ref, sf_ref = _run("plain", inp, False)
