@@ -194,16 +194,21 @@ cudaError_t deltanet_chunk_prefill_gated_noalloc(
 cudaError_t deltanet_noalloc_read_status(int* status_host, int clear, cudaStream_t stream);
 
 /* Copy the device status word of a workspace to *status_host (synchronises
- * `stream`). 0 = clean; bit 0 = a bounded wait timed out. Clears it when
- * clear != 0. No counterpart in the reference (its kernels have no waits). */
+ * `stream`). 0 = clean; bit 0 = a bounded wait timed out (each wait gives up
+ * after about 1 s). The bits above say which part gave up: 8-11 the
+ * cluster-split kernel's chain CTA (compute warps, MMA warp, load warp, output
+ * MMA warp), 12-13 its prep CTAs (compute warps, gate warp), 14 its output CTA,
+ * 15 the one-CTA-per-head kernel. Clears it when clear != 0. No counterpart in
+ * the reference (its kernels have no waits). */
 cudaError_t deltanet_read_status(void* workspace, int* status_host, int clear, cudaStream_t stream);
 
 /* Test hook for failure detection; no counterpart in the reference (its
  * kernels have no waits; its error convention is the return code,
  * kernels/chunk_delta_cuda.cu:706-727). Runs deltanet_chunk_prefill_gated with
  * the v-tile load of chunk `withheld_chunk` never issued, so that the kernel's
- * bounded wait for that tile runs out (~0.3 s): the kernel sets bit 0 of the
- * workspace status word, stops its loop, waits (bounded) for the copies and
+ * bounded wait for that tile runs out (about 1 s): the kernel sets bit 0 of
+ * the workspace status word (and the bit of the role that gave up, see
+ * deltanet_read_status), stops its loop, waits (bounded) for the copies and
  * MMAs it has in flight, frees its tensor memory and returns; y and
  * final_state are then undefined. kernel: 0 = the launcher's choice, 1 = one
  * CTA per (sequence, v-head), 2 = the cluster-split kernel

@@ -245,9 +245,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     // Every wait is bounded; a timeout records status bit 0 and stops the CTA.
     // issued[] / consumed[] count barrier completions so the exit path can
     // drain whatever is still in flight (thread 0 issues every TMA and MMA).
+    // A failure is recorded as bit 0 plus bit 15 (this kernel) of the status word. Loads are
+    // issued only while no failure is recorded: after a failed wait the phase waited for may
+    // still be pending, and a new load would arm it a second time.
     auto fail = [&]() {
         *abort_flag = 1;
-        if (p.status) atomicOr(p.status, 1u);
+        if (p.status) atomicOr(p.status, 1u | (1u << 15));
     };
     auto wait_bar = [&](int i, uint32_t parity) {
         if (ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) ++consumed[i];
@@ -472,7 +475,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             }
             if (phase == 2) {
                 asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 4-7 are done with the z tile
-                if (tid == 128 && n + 1 < NC) {
+                if (tid == 128 && n + 1 < NC && !*abort_flag) {
                     ptx::fence_proxy_async_smem();
                     load_z(n + 1);
                 }
@@ -585,7 +588,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             commit();
         }
         wait_mma();
-        if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk) load_v(n + 1);  // v tile consumed
+        if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk && !*abort_flag) load_v(n + 1);  // v tile consumed
         {   // v_new^T (fp32, cols TM_C12) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
             {
@@ -681,7 +684,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         }
         wait_bar(BAR_O1, consumed[BAR_O1] & 1u);  // S^T q^T has read the old state operand and q
         ptx::tc_fence_after();
-        if (tid == 0 && n + 1 < NC) {  // q and k tiles consumed (k by dS)
+        if (tid == 0 && n + 1 < NC && !*abort_flag) {  // q and k tiles consumed (k by dS)
             load_q(n + 1);
             load_k(n + 1);
         }

@@ -219,16 +219,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     // are of the TMA tiles and slot fills a thread arms (scalars, for the abort-path drain):
     // counters in an array indexed by slot parity would live in local memory, and with most
     // of the SM's L1 given to shared memory each update is a round trip to L2.
+    //
+    // Abort protocol. A wait that runs out sets the CTA's flag and records its role in the
+    // status word (bit 0, plus 8-11: chain compute / MMA / load / output-MMA warps, 12-13: prep
+    // compute / gate warps, 14: output CTA). Once the flag is set, no thread of the CTA arms a
+    // barrier or issues a TMA load, MMA or bulk copy that it has not issued already: the phase
+    // a failed wait was for may still be pending, and arming a pending phase (an arrival it has
+    // no count for) or shipping into a peer's slot that was not armed is undefined. Single-
+    // thread roles leave their loop at once; warps 0-7, which share named barriers, carry on to
+    // their next vote (their own arrivals are on count barriers without transaction bytes) and
+    // leave together.
     auto fail = [&]() {
         *abort_flag = 1;
-        if (p.status) atomicOr(p.status, 1u);
+        if (p.status) {  // the role, recomputed here (cold path) rather than kept in a register
+            const uint32_t w = threadIdx.x >> 5, r = ptx::cluster_ctarank();
+            const uint32_t role = r == CHAIN_RANK ? (w < (uint32_t)ISSUER_WARP ? 8u : 9u + (w - ISSUER_WARP))
+                                                  : (r == OUT_RANK ? 14u : (w < (uint32_t)ISSUER_WARP ? 12u : 13u));
+            atomicOr(p.status, 1u | (1u << role));
+        }
     };
-    auto wait_bar = [&](int i, uint32_t parity) {
-        if (!ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) fail();
+    auto wait_bar = [&](int i, uint32_t parity) -> bool {
+        if (ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) return true;
+        fail();
+        return false;
     };
-    auto wait_mma = [&](uint32_t parity) {
-        wait_bar(B_MMA, parity);
+    auto wait_mma = [&](uint32_t parity) -> bool {
+        const bool ok = wait_bar(B_MMA, parity);
         ptx::tc_fence_after();
+        return ok;
     };
     auto commit_to = [&](int b) { ptx::mma_commit(bar(b)); };
     // abort path: wait (bounded) for the last phase armed on a barrier (re-armed only after
@@ -484,7 +502,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
                 wait_bar(B_Q, ph);
                 wait_bar(B_K, ph);
-                if (tid == 0) {
+                if (tid == 0 && !*abort_flag) {
                     ptx::tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < 8; ++s) {
@@ -498,7 +516,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 csync();
                 wait_bar(B_GREADY + (k & 1), (uint32_t)((k >> 1) & 1));  // gates (L, M need them; P1 does not)
                 wait_mma(0u);  // P1: the CTA's commits alternate P1 (even phases) and P3 (odd)
-                if (tid == 0 && n + NP < NC) load_q(n + NP);  // P1 has read q
+                if (tid == 0 && !*abort_flag && n + NP < NC) load_q(n + NP);  // P1 has read q
                 {   // rows 0-63: M = scale (q_i k_j) e^{c_i - c_j}, j <= i (hi/lo -> staging);
                     // rows 64-127: L = beta_i (k_i k_j) e^{c_i - c_j}, j < i (fp32 scratch).
                     // One loop for both, so that the loop body's code stays small.
@@ -564,7 +582,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 ptx::fence_proxy_async_smem();
                 csync();
                 if (tid == 0) ptx::mbar_arrive(bar(B_GFREE + (k & 1)));  // gate slot read
-                if (tid == 0) {  // P3: W^T = K^T [T''_hi; T''_lo]^T
+                if (tid == 0 && !*abort_flag) {  // P3: W^T = K^T [T''_hi; T''_lo]^T
                     ptx::tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
@@ -575,7 +593,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     commit();
                 }
                 wait_mma(1u);  // P3
-                if (tid == 0 && n + NP < NC) {  // k consumed: fetch this CTA's next chunk
+                if (tid == 0 && !*abort_flag && n + NP < NC) {  // k consumed: fetch this CTA's next chunk
                     load_k(n + NP);
                     prefetch_tile(&p.tm_q, hq, n + 2 * NP);
                     prefetch_tile(&p.tm_k, hq, n + 2 * NP);
@@ -597,14 +615,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 ptx::tc_fence_before();
                 ptx::fence_proxy_async_smem();
                 csync();
-                if (tid == 0) {  // ship each part once the chain has handed back that part of the previous chunk
+                if (tid == 0 && !*abort_flag) {  // ship each part once the chain has handed back that part of the previous chunk
                     // A part is shipped only if its hand-back arrived: after a wait that ran out, the chain's
                     // slot is not armed, and the copy could still be in flight when the cluster exits.
-                    auto wait_empty = [&](int b) {
-                        if (ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) return true;
-                        fail();
-                        return false;
-                    };
+                    auto wait_empty = [&](int b) { return !*abort_flag && wait_bar(b, (uint32_t)((k - 1) & 1)); };
                     // the chain CTA's slots and barriers sit at its own offsets, in CTA CHAIN_RANK
                     const uint32_t fa = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLA + pi), CHAIN_RANK);
                     const uint32_t fbb = ptx::mapa(sb + C_MISC + M_BAR + 8u * (uint32_t)(B_FULLB + pi), CHAIN_RANK);
@@ -659,7 +673,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     }
                 }
                 csync();  // o slot read, o staged
-                if (tid == 0) {
+                if (tid == 0 && !*abort_flag) {  // (after a failed wait the slot's phase may be pending: not re-armed)
                     if (n + 2 < NC) {  // this parity's slot takes chunk n + 2
                         if (n & 1) ++armed_o1;
                         else ++armed_o0;
@@ -716,7 +730,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         dst[eq + 4 * m] = make_uint4(outw[4 * m], outw[4 * m + 1], outw[4 * m + 2], outw[4 * m + 3]);
                 }
                 csync();  // o and z tile read
-                if (tid == 0 && p.gated && n + 2 < NC) {  // this parity's z tile takes chunk n + 2
+                if (tid == 0 && !*abort_flag && p.gated && n + 2 < NC) {  // this parity's z tile takes chunk n + 2
                     ptx::fence_proxy_async_smem();
                     load_zt(n + 2);
                     prefetch_tile(&p.tm_z, h, n + 3);
@@ -770,9 +784,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // ---------------- MMA issue. tcgen05.mma occupies the issuing thread for about the
             // instruction's execution time, so this warp issues MMAs and waits only on what
             // gates them; loads and slot hand-backs run on the producer warp.
-            auto wait_full = [&](int b, int m) {
-                if (!ptx::mbar_wait(bar(b + m % NSLOT), slot_par(m), WAIT_ITERS)) fail();
-            };
+            // A failed wait ends the loop: no MMA is issued on a tile or operand that did not arrive.
             if (lane == 0) {
                 for (int n = 0; n < NC; ++n) {
                     if (*abort_flag) break;
@@ -780,9 +792,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     const uint32_t sp = aslot(n);
                     // ---- C12: v_new^T = v^T [T'_hi;T'_lo]^T - S^T [W_hi|W_lo] (hi terms cols 0-63, lo 64-127);
                     //      the v^T T'^T part does not depend on the state and goes first
-                    wait_full(B_FULLA, n);
-                    wait_bar(B_V, ph);
-                    if (n > 0) wait_bar(B_TSFREE, (uint32_t)((n - 1) & 1));  // dS of chunk n-1 read
+                    if (!wait_bar(B_FULLA + n % NSLOT, slot_par(n)) || !wait_bar(B_V, ph)) break;
+                    if (n > 0 && !wait_bar(B_TSFREE, (uint32_t)((n - 1) & 1))) break;  // dS of chunk n-1 read
                     ptx::tc_fence_after();
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
@@ -791,7 +802,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         ptx::mma_bf16(tmem + T_C12, a, b, ID_U, s > 0);
                     }
                     commit_to(B_VT);      // the v tile is free once these have run
-                    wait_bar(B_SOP, ph);  // S_n^T hi/lo in TMEM
+                    if (!wait_bar(B_SOP, ph)) break;  // S_n^T hi/lo in TMEM
                     ptx::tc_fence_after();
 #pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
@@ -807,8 +818,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     }
                     commit();
                     // ---- dS^T = (v_new e^{cL-c})^T K, once v_new is in TMEM
-                    wait_bar(B_K, ph);
-                    wait_bar(B_VNR, ph);
+                    if (!wait_bar(B_K, ph) || !wait_bar(B_VNR, ph)) break;
                     ptx::tc_fence_after();
 #pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
@@ -828,14 +838,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // ---------------- MMA issue for the output terms, off the state recurrence: S^T q^T
             // while warps 0-7 form v_new (after C12), v_new^T M^T while they update the state
             // (after dS), so that their issue time does not delay C12 and dS on warp 8.
-            if (lane == 0) {
+            if (lane == 0) {  // a failed wait ends the loop, as on warp 8
                 for (int n = 0; n < NC; ++n) {
                     if (*abort_flag) break;
                     const uint32_t ph = (uint32_t)(n & 1);
                     // ---- o1^T = S^T q^T, once the previous chunk's output accumulators are read
-                    wait_bar(B_MMA, ph);  // C12 done: the tensor core is free while v_new is formed
-                    wait_bar(B_Q, ph);
-                    if (n > 0) wait_bar(B_OFREE, (uint32_t)((n - 1) & 1));
+                    if (!wait_bar(B_MMA, ph) || !wait_bar(B_Q, ph)) break;  // C12 done: the tensor core is free
+                    if (n > 0 && !wait_bar(B_OFREE, (uint32_t)((n - 1) & 1))) break;
                     ptx::tc_fence_after();
 #pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
@@ -848,9 +857,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     }
                     commit_to(B_X2);
                     // ---- o2^T = v_new^T M^T, once dS is done
-                    wait_bar(B_X1, ph);
-                    wait_bar(B_VNR, ph);
-                    if (!ptx::mbar_wait(bar(B_FULLB + n % NSLOT), slot_par(n), WAIT_ITERS)) fail();
+                    if (!wait_bar(B_X1, ph) || !wait_bar(B_VNR, ph) || !wait_bar(B_FULLB + n % NSLOT, slot_par(n))) break;
                     ptx::tc_fence_after();
                     const uint32_t bp = bslot(n);
 #pragma unroll 1
@@ -874,24 +881,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 load_q(0);
                 load_k(0);
                 if (p.withhold_v_chunk != 0) load_v(0);
+                // A failed wait ends the loop, and so does a failure of warps 0-7 (their flag is
+                // released by the hand-off arrival this warp has just acquired): no tile is loaded
+                // and no slot is re-armed while its previous phase may be pending.
                 for (int n = 0; n < NC; ++n) {
                     if (*abort_flag) break;
                     const uint32_t ph = (uint32_t)(n & 1);
-                    wait_bar(B_VT, ph);  // v^T T'^T has read the v tile
+                    if (!wait_bar(B_VT, ph)) break;  // v^T T'^T has read the v tile
                     if (n + 1 < NC && n + 1 != p.withhold_v_chunk) load_v(n + 1);
                     prefetch_tile(&p.tm_v, h, n + 2);
-                    wait_bar(B_VNR, ph);  // C12 read part A; decay factors copied
+                    if (!wait_bar(B_VNR, ph) || *abort_flag) break;  // C12 read part A; decay factors copied
                     if (n + NSLOT < NC) arm_slot(B_FULLA, n, A_BYTES);
                     ptx::mbar_arrive_remote(prep_bar(B_EMPTYA, n));
-                    wait_bar(B_X1, ph);  // dS done: k tile free
-                    wait_bar(B_X2, ph);  // S^T q^T done: q tile free
+                    if (!wait_bar(B_X1, ph) || !wait_bar(B_X2, ph)) break;  // dS, S^T q^T done: k, q tiles free
                     if (n + 1 < NC) {
                         load_q(n + 1);
                         load_k(n + 1);
                     }
                     prefetch_tile(&p.tm_q, hq, n + 2);
                     prefetch_tile(&p.tm_k, hq, n + 2);
-                    wait_bar(B_Y, ph);  // v_new^T M^T done: part B free
+                    if (!wait_bar(B_Y, ph)) break;  // v_new^T M^T done: part B free
                     if (n + NSLOT < NC) arm_slot(B_FULLB, n, B_BYTES);
                     ptx::mbar_arrive_remote(prep_bar(B_EMPTYB, n));
                 }
@@ -913,7 +922,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             const int pi = (int)rank - (int)PREP_RANK0;
             int k = 0;
             for (int n = pi; n < NC; n += NP, ++k) {
-                if (*abort_flag) break;
+                if (__any_sync(0xffffffffu, *abort_flag != 0)) break;  // one decision for the warp (shuffles below)
                 if (k >= 2) wait_bar(B_GFREE + (k & 1), (uint32_t)(((k >> 1) - 1) & 1));
                 const int valid = min(CS, len - n * CS);
                 const long long t0 = tok_base + (long long)n * CS;

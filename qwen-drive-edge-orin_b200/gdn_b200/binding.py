@@ -278,6 +278,27 @@ def segment_entry_states(Phi, A, s0=None):
     return torch.stack(states, dim=1).view(B, HV, nseg, d, d).transpose(1, 2).float().contiguous()
 
 
+_seg_lock = threading.Lock()
+_seg_cache: dict = {}
+
+
+def _segment_constants(dev, cu, N, HV, v_shape):
+    """Device constants of one segmentation, built once and reused: the int32 offsets, the
+    identity entry states and the zero v of the state-map pass (building them per call costs a
+    synchronous host-to-device copy and two allocations)."""
+    key = (dev, cu, N, HV, v_shape)
+    with _seg_lock:
+        c = _seg_cache.get(key)
+        if c is None:
+            if len(_seg_cache) > 16:
+                _seg_cache.clear()
+            cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+            eye = torch.eye(HEAD_DIM, device=dev, dtype=torch.float32).expand(N, HV, HEAD_DIM, HEAD_DIM).contiguous()
+            c = (cu_t, eye, torch.zeros(v_shape, dtype=torch.bfloat16, device=dev))
+            _seg_cache[key] = c
+        return c
+
+
 def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: float = 1e-6,
                             segments: int | None = None):
     """Prefill of long sequences cut into segments that run in parallel: [o or y, final_state].
@@ -309,10 +330,9 @@ def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: floa
     N = B * per_seq
     pk = lambda t: t.contiguous().reshape(1, B * T, *t.shape[2:])  # noqa: E731  (packed, B = 1)
     qp, kp, vp, gp, bp = (pk(t) for t in (q, k, v, g, beta))
-    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    cu_t, eye, v_zero = _segment_constants(dev, tuple(cu), N, HV, tuple(vp.shape))
     _, A = chunk_prefill_varlen(qp, kp, vp, gp, bp, cu_t)
-    eye = torch.eye(HEAD_DIM, device=dev, dtype=torch.float32).expand(N, HV, HEAD_DIM, HEAD_DIM).contiguous()
-    _, Phi = chunk_prefill_varlen(qp, kp, torch.zeros_like(vp), gp, bp, cu_t, s0=eye)
+    _, Phi = chunk_prefill_varlen(qp, kp, v_zero, gp, bp, cu_t, s0=eye)
     s0 = None if s0 is None else _state(s0, (B, HV, HEAD_DIM, HEAD_DIM), dev)
     starts = segment_entry_states(Phi.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM),
                                   A.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM), s0)

@@ -1,6 +1,6 @@
 """Failure detection on the GPU without a GPU fault.
 
-Every mbarrier wait in the prefill kernels is bounded (~0.3 s). The test hook
+Every mbarrier wait in the prefill kernels is bounded (about 1 s). The test hook
 ``deltanet_test_withheld_load`` runs the gated prefill with one v-tile TMA load never
 issued: a producer that never arrives. The consumer's wait must run out, the kernel must
 record bit 0 in the workspace status word, stop, wait (bounded) for the copies and MMAs it
