@@ -148,6 +148,14 @@ class ClockSampler:
             self._stop.set()
             self._t.join()
 
+    def read_mhz(self):
+        if not self.ok:
+            return None
+        try:
+            return self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+        except Exception:
+            return None
+
     def summary(self):
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
@@ -255,19 +263,32 @@ class Workload:
         return gdn_b200.chunk_prefill_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["z"], d["w"], d.get("s0"))
 
 
-def time_windows(wl, sets, outs, stream, steps, n_windows):
-    """ms per step of ``n_windows`` consecutive windows of ``steps`` steps, launched back to back
-    with an event at each boundary (inputs rotate over ``sets``)."""
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_windows + 1)]
-    evs[0].record(stream)
-    i = 0
-    for w in range(n_windows):
-        for _ in range(steps):
-            wl.step(sets[i % len(sets)], outs[i % len(sets)], stream)
-            i += 1
-        evs[w + 1].record(stream)
+GATE_CYCLES = 4_000_000  # ~2 ms of device spin ahead of a timed window
+
+
+def time_window(wl, sets, outs, stream, steps, start=0):
+    """ms per step of one window of ``steps`` steps (inputs rotate over ``sets``). A short device
+    spin is queued ahead of the first event, so that the host has enqueued the window's launches
+    before the first one starts: the events then time the device's work, not the host's pace."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(GATE_CYCLES)
+    e0.record(stream)
+    for i in range(start, start + steps):
+        wl.step(sets[i % len(sets)], outs[i % len(sets)], stream)
+    e1.record(stream)
     torch.cuda.synchronize()
-    return [evs[w].elapsed_time(evs[w + 1]) / steps for w in range(n_windows)]
+    return e0.elapsed_time(e1) / steps
+
+
+def time_windows(wl, sets, outs, stream, steps, n_windows, clk=None):
+    """``n_windows`` repeats of the timed window: ms per step of each, and the SM clock read
+    right after each window (the device was busy until a few microseconds before)."""
+    ms, mhz = [], []
+    for w in range(n_windows):
+        ms.append(time_window(wl, sets, outs, stream, steps, w * steps))
+        mhz.append(clk.read_mhz() if clk is not None else None)
+    return ms, mhz
 
 
 def max_over_ranks(x, dist, device):
@@ -333,7 +354,7 @@ def time_config4(device, steps):
     for _ in range(3):
         wl.step(wl.inp, out, stream)
     torch.cuda.synchronize()
-    ms = time_windows(wl, [wl.inp], [out], stream, steps, 1)[0]
+    ms = time_window(wl, [wl.inp], [out], stream, steps)
     hbm_gbs = load_peaks()[0]
     gbs = wl.step_bytes / (ms / 1e3) / 1e9
     res = {"workload": CONFIGS[4]["desc"], "ms_per_step": round(ms, 4), "steps": steps,
@@ -437,14 +458,8 @@ def main():
         est_ms = 1.0 if args.config == 4 else 4.0
         n_extra = max(2, min(n_extra, int(10_000 / max(1.0, args.steps * est_ms))))
     with ClockSampler(local) as clk:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(args.steps):
-            wl.step(sets[i % n_sets], outs[i % n_sets], stream)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms_total = e0.elapsed_time(e1)
-        win = time_windows(wl, sets, outs, stream, args.steps, n_extra) if n_extra else []
+        ms_total = time_window(wl, sets, outs, stream, args.steps) * args.steps
+        win, win_mhz = time_windows(wl, sets, outs, stream, args.steps, n_extra, clk) if n_extra else ([], [])
     ms_total = max_over_ranks(ms_total, dist, device)
     win = max_over_ranks(win, dist, device) if win else []
     if dist:
@@ -457,7 +472,8 @@ def main():
     if win:
         windows = {"n": len(win), "steps_each": args.steps, "ms_per_step_median": round(statistics.median(win), 5),
                    "ms_per_step_min": round(min(win), 5), "ms_per_step_max": round(max(win), 5),
-                   "tokens_per_s_median": round(wl.job_tokens / (statistics.median(win) / 1e3), 1)}
+                   "tokens_per_s_median": round(wl.job_tokens / (statistics.median(win) / 1e3), 1),
+                   "sm_mhz_after_each": win_mhz}
 
     # config 1: the same launches replayed from a CUDA graph (what is left is GPU-side launch cost)
     graph = None

@@ -7,7 +7,8 @@ kernels/chunk_delta_cuda_tco.cu, the production bf16 o-pass) into
 (kernels/harness/parity_cuda.py:75-98: row cosine >= 0.999 and floored max-rel < 1e-2 on
 o and the state) applied between the reference's kernels and ours on identical inputs,
 plus the north-star bars (o max-abs <= 2e-2, state relative L2 <= 1e-2). Both sides are
-timed with CUDA events (median of five calls after two warm-ups), and the timings are
+timed through their C ABI with buffers allocated beforehand, with CUDA events (median of
+five calls after two warm-ups, ungated, as the reference's contract), and the timings are
 reported as a pytest warning so that they appear in the run's summary.
 
 Skipped when ``oracle/_ref`` holds no build (it needs the reference checkout at build time).
@@ -91,12 +92,19 @@ def test_agrees_with_reference_cuda_kernels(cfg):
         s0 = n(B, HV, D, D) * 0.02
     o, sf = gdn_b200.chunk_prefill(q, k, v, g, beta, s0)
     torch.cuda.synchronize()
-    ours_us = _time(lambda: gdn_b200.chunk_prefill(q, k, v, g, beta, s0))
+    # ours timed the way theirs is: through the C ABI with the buffers allocated beforehand
+    ours = gdn_b200.load_library()
+    vp = ctypes.c_void_p
+    stream = vp(torch.cuda.current_stream().cuda_stream)
+    o_t, sf_t = torch.empty_like(v), torch.empty(B, HV, D, D, device="cuda")
+    ws_t = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    ours_us = _time(lambda: ours.deltanet_chunk_prefill(  # noqa: E731
+        vp(q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()), vp(g.data_ptr()), vp(beta.data_ptr()),
+        vp(o_t.data_ptr()), vp(s0.data_ptr()), vp(sf_t.data_ptr()), B, T, HV, HQK, D, D, 64, vp(ws_t.data_ptr()),
+        256, stream, 0))
     nb = B if cfg == "config1" else 4  # sequences compared (config 4: the first four of 32)
     host = lambda t: t[:nb].float().cpu().numpy()  # noqa: E731
     o_h, sf_h = host(o), host(sf)
-    vp = ctypes.c_void_p
-    stream = vp(torch.cuda.current_stream().cuda_stream)
     lines = [f"{cfg}: ours {ours_us:.1f} us"]
     for pre, name in (("deltanet", "canonical"), ("deltanet_tcop", "tco")):
         nbytes = getattr(lib, f"{pre}_prefill_workspace_size")(B, T, HV, D, D, 64)
