@@ -435,7 +435,10 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
+        # keep rank 0's stdout to the one JSON line: NCCL prints its version banner at WARN and
+        # above, to stdout unless told otherwise
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     wl = Workload(args.config, rank, world, device)
