@@ -223,8 +223,13 @@ class Workload:
         self.step_bytes = alg_bytes(B, T, HQK, HV, with_s0=cfg["s0"])
         self.step_flops = alg_flops(B, T, HV)
         self.segmented = cfg["shard"] == "head"
-        self.launches_per_step = 3 if self.segmented else 1
-        self.ws = torch.zeros(256, dtype=torch.uint8, device=device)
+        ws_bytes = 256
+        if self.segmented:  # the library's segment choice for this shape and device (256 B: one pass)
+            import gdn_b200
+            ws_bytes = max(256, int(gdn_b200.load_library().deltanet_segmented_workspace_size(
+                B, T, HV, D, D, 64, 0)))
+        self.launches_per_step = 3 if ws_bytes > 256 else 1
+        self.ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
 
     def outputs(self):
         return torch.empty_like(self.inp["v"]), torch.empty(self.B, self.HV, D, D, device=self.device)
@@ -235,16 +240,18 @@ class Workload:
 
         import gdn_b200
         y, sf = out
-        if self.segmented:  # long streams: segments side by side (gdn_b200.chunk_prefill_segmented)
-            with torch.cuda.stream(stream):
-                yy, ss = gdn_b200.chunk_prefill_segmented(s["q"], s["k"], s["v"], s["g"], s["beta"], s["s0"],
-                                                          z=s["z"], w=s["w"])
-                y.copy_(yy)
-                sf.copy_(ss)
-            return
         vp = ctypes.c_void_p
         lib = gdn_b200.load_library()
         s0 = s["s0"]
+        if self.segmented:  # long streams: segments side by side, the library's segment choice
+            rc = lib.deltanet_chunk_prefill_segmented(
+                vp(s["q"].data_ptr()), vp(s["k"].data_ptr()), vp(s["v"].data_ptr()), vp(s["g"].data_ptr()),
+                vp(s["beta"].data_ptr()), vp(s["z"].data_ptr()), vp(s["w"].data_ptr()), 1e-6, vp(y.data_ptr()),
+                vp(0 if s0 is None else s0.data_ptr()), vp(sf.data_ptr()), self.B, self.T, self.HV, self.HQK, D, D,
+                64, 0, vp(self.ws.data_ptr()), self.ws.numel(), vp(stream.cuda_stream))
+            if rc != 0:
+                raise RuntimeError(f"deltanet_chunk_prefill_segmented returned {rc}")
+            return
         rc = lib.deltanet_chunk_prefill_gated(vp(s["q"].data_ptr()), vp(s["k"].data_ptr()), vp(s["v"].data_ptr()),
                                               vp(s["g"].data_ptr()), vp(s["beta"].data_ptr()), vp(s["z"].data_ptr()),
                                               vp(s["w"].data_ptr()), 1e-6, vp(y.data_ptr()),
@@ -531,9 +538,9 @@ def main():
                 "frac_of_roofline_time": round(max(step_bytes / (hbm_gbs * 1e9), flops / (tf_burst * 1e12))
                                                / (ms_step / 1e3), 4),
                 "kernel": traffic_kernel}
-    if wl.segmented:
-        roofline["note"] = ("per rank, whole step (three segmented passes and the entry-state scan); "
-                            "algorithmic bytes of one pass")
+    if wl.launches_per_step > 1:
+        roofline["note"] = ("per rank, whole step (state pass, entry-state scan, output pass of the segmented "
+                            "call); algorithmic bytes of one pass")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -624,7 +631,7 @@ def run_e2e(args, wl, device, dist):
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), dist, device)
     ms_step = ms / steps
-    api = ("gdn_b200.chunk_prefill_segmented (ctypes -> deltanet_chunk_prefill_varlen x3)" if wl.segmented
+    api = ("gdn_b200.chunk_prefill_segmented (ctypes -> deltanet_chunk_prefill_segmented)" if wl.segmented
            else "gdn_b200.chunk_prefill_gated (ctypes -> deltanet_chunk_prefill_gated)")
     return {"value": round(wl.job_tokens / (ms_step / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_step, 4), "steps": steps, "api": api,

@@ -109,6 +109,32 @@ cudaError_t deltanet_chunk_prefill_varlen(
     void* workspace, size_t workspace_bytes,
     cudaStream_t stream);
 
+/* Long sequences in segments; no counterpart in the reference (its state carry
+ * walks every chunk of a sequence in one serial loop, kernels/chunk_delta_cuda.cu:312-424).
+ * Same inputs, outputs and results as deltanet_chunk_prefill (z and norm_w NULL:
+ * `out` receives o) or deltanet_chunk_prefill_gated (both set: `out` receives y),
+ * for few long sequences, where one pass leaves most of the GPU idle on the serial
+ * chunk recurrence. Each sequence is cut at chunk boundaries into `segments`
+ * segments (0: chosen for the current device from a wave model, 1 or a full GPU:
+ * one pass) and three launches run on `stream`: every segment from a zero state
+ * and from the identity with v = 0 (final states A_j and Phi_j, one grid), the
+ * scan S_0 = initial_state, S_{j+1} = Phi_j S_j + A_j of the segments' entry
+ * states, and every segment from its entry state (the output, and the final
+ * state of the last segment). The workspace must hold
+ * deltanet_segmented_workspace_size(...) bytes for the same arguments and device
+ * (256 when one pass is chosen). */
+size_t deltanet_segmented_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size, int segments);
+cudaError_t deltanet_chunk_prefill_segmented(
+    const void* q, const void* k, const void* v,
+    const float* g, const float* beta,
+    const void* z, const void* norm_w, float eps,
+    void* out,
+    const float* initial_state,
+    float* final_state,
+    int B, int T, int HV, int HQK, int DK, int DV, int chunk_size, int segments,
+    void* workspace, size_t workspace_bytes,
+    cudaStream_t stream);
+
 /* Inputs of the reference's TRT prefill adapter: the GDNParams fields that
  * runGdnChunkPrefillSm87 reads (gdnChunkPrefillSm87.cu:188-230), plus an
  * optional fused gated RMSNorm and the workspace. */

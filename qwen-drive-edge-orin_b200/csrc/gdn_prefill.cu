@@ -860,7 +860,9 @@ static cudaError_t ensure_smem_attr() {
 
 constexpr size_t WS_HEADER = 256;
 
-cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream);  // gdn_prefill_split.cu
+cudaError_t launch_split(const Params& p, int nseq, int grid_heads, cudaStream_t stream);  // gdn_prefill_split.cu
+cudaError_t launch_segment_scan(const float* stt, const float* s0, float* entry, int B, int HV, int nseg,
+                                cudaStream_t stream);  // gdn_segment_scan.cu
 int split_cluster_ctas();
 bool split_available();
 
@@ -910,6 +912,14 @@ struct Launch {
     // 2 cluster split) and the chunk whose v-tile load is withheld (-1 none)
     int force_kernel;
     int withhold_v_chunk;
+    // segmented passes (deltanet_chunk_prefill_segmented; cluster-split kernel): chunks per
+    // segment and segments per sequence (nseq = B * seg_per_seq); the state pass (2 HV heads
+    // in the grid, zero tile v0 for the identity runs, no output) or the output pass (only the
+    // last segment's final state, at sf[b])
+    int seg_chunks, seg_per_seq;
+    int state_pass;
+    const void* v0;
+    int sf_last_only;
 };
 
 // A Launch with every field cleared and no test hook armed.
@@ -924,13 +934,14 @@ static cudaError_t launch(const Launch& L) {
     if (L.DK != HD || L.DV != HD || L.chunk != CS) return cudaErrorInvalidValue;
     if (L.HQK <= 0 || L.HV <= 0 || L.HV % L.HQK != 0) return cudaErrorInvalidValue;
     if (L.T < 0 || L.nseq < 0 || L.HV > 65535 || L.nseq > 65535) return cudaErrorInvalidValue;
-    if (!L.q || !L.k || !L.v || !L.out || !L.sf || !L.ws) return cudaErrorInvalidValue;
+    if (!L.q || !L.k || !L.v || (!L.out && !L.state_pass) || !L.sf || !L.ws) return cudaErrorInvalidValue;
+    if (L.state_pass && (!L.v0 || L.seg_chunks <= 0 || L.s0)) return cudaErrorInvalidValue;
     if (L.prestage ? (!L.ga || !L.gb || !L.A_log || !L.dt_bias) : (!L.g || !L.beta)) return cudaErrorInvalidValue;
     if (L.ws_bytes < WS_HEADER) return cudaErrorInvalidValue;
     const bool gated = (L.z != nullptr) || (L.w != nullptr);
     if (gated && (!L.z || !L.w)) return cudaErrorInvalidValue;
     if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || (gated && !aligned16(L.z)) ||
-        !aligned16(L.ws) || !aligned16(L.out))
+        !aligned16(L.ws) || !aligned16(L.out) || !aligned16(L.v0))
         return cudaErrorInvalidValue;
     if (L.nseq == 0 || L.HV == 0) return cudaSuccess;
 
@@ -969,6 +980,19 @@ static cudaError_t launch(const Launch& L) {
     p.A_log = L.A_log;
     p.dt_bias = static_cast<const __half*>(L.dt_bias);
     p.withhold_v_chunk = L.withhold_v_chunk;
+    p.seg_chunks = L.seg_chunks;
+    p.seg_per_seq = L.seg_per_seq;
+    p.sf_last_only = L.sf_last_only;
+    if (L.seg_chunks > 0) {  // segmented passes: cluster-split kernel only (the caller checked it can run)
+        if (L.dbg || L.prestage || L.cu || L.nseq != L.B * L.seg_per_seq) return cudaErrorInvalidValue;
+        if (L.state_pass) {
+            if (!make_map(&p.tm_v0, L.v0, 1, CS, 1)) return cudaErrorInvalidValue;  // one zero tile
+        } else {
+            p.tm_v0 = p.tm_v;
+        }
+        return launch_split(p, L.nseq, L.state_pass ? 2 * L.HV : L.HV, L.stream);
+    }
+    p.tm_v0 = p.tm_v;
 
     const bool split = !L.dbg && !L.prestage && use_split(L.nseq, L.HV, L.force_kernel);
     if (L.force_kernel == 2 && !split) return cudaErrorNotSupported;
@@ -1023,6 +1047,61 @@ static cudaError_t noalloc_scratch(void** out) {
     return cudaSuccess;
 }
 
+// ---------------------------------------------------------------------------
+// Long sequences in segments (deltanet_chunk_prefill_segmented).
+constexpr size_t SEG_ZERO_BYTES = (size_t)CS * HD * 2;  // one zero bf16 tile [64 tok][128]: the identity runs' v
+
+// Segments per sequence for B sequences of NC chunks and HV v-heads on `sms` SMs, from a wave
+// model of the cluster-split kernel (4-CTA clusters, sms / 4 per wave, one chunk period per
+// chunk): the segmented call costs (waves of 2 U s units + waves of U s units) * ceil(NC / s)
+// chunk periods, U = B HV (state pass, then output pass; the scan is small), against
+// waves(U) * NC for one pass. Returns the cheapest s (1: one pass), the smaller on ties.
+static int auto_segments(int B, int HV, int NC, int sms) {
+    const long long wave = sms / split_cluster_ctas(), U = (long long)B * HV;
+    if (wave <= 0 || NC <= 1) return 1;
+    auto waves = [&](long long units) { return (units + wave - 1) / wave; };
+    long long best_cost = waves(U) * NC;
+    int best = 1;
+    for (int s = 2; s <= NC && s <= 256; ++s) {
+        const long long per = (NC + s - 1) / s;
+        const long long eff = (NC + per - 1) / per;  // segments actually made with `per` chunks each
+        if (eff != s) continue;
+        const long long cost = (waves(2 * U * s) + waves(U * s)) * per;
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    return best;
+}
+
+// (segments per sequence, chunks per segment) actually used for a request of `segments`
+// (0: automatic on the current device).
+static void resolve_segments(int B, int T, int HV, int segments, int* nseg, int* per) {
+    const int NC = (T + CS - 1) / CS;
+    int s = segments;
+    if (s <= 0) {
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            sms = 0;
+        s = auto_segments(B, HV, NC, sms);
+    }
+    if (NC <= 1 || s <= 1) {
+        *nseg = 1;
+        *per = NC;
+        return;
+    }
+    s = s < NC ? s : NC;
+    *per = (NC + s - 1) / s;
+    *nseg = (NC + *per - 1) / *per;
+}
+
+static size_t segmented_bytes(int B, int HV, int nseg) {
+    if (nseg <= 1) return WS_HEADER;
+    return WS_HEADER + SEG_ZERO_BYTES + (size_t)B * nseg * 3 * HV * HD * HD * sizeof(float);
+}
+
 static size_t debug_bytes(int B, int T, int HV) {
     const size_t nc = (size_t)((T + CS - 1) / CS);
     return (size_t)B * HV * nc * DBG_REC * sizeof(float);
@@ -1038,6 +1117,14 @@ extern "C" {
 size_t deltanet_prefill_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size) {
     (void)B; (void)T; (void)HV; (void)DK; (void)DV; (void)chunk_size;
     return gdn::WS_HEADER;
+}
+
+size_t deltanet_segmented_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size, int segments) {
+    (void)DK; (void)DV; (void)chunk_size;
+    if (B <= 0 || T <= 0 || HV <= 0) return gdn::WS_HEADER;
+    int nseg = 1, per = 1;
+    gdn::resolve_segments(B, T, HV, segments, &nseg, &per);
+    return gdn::segmented_bytes(B, HV, nseg);
 }
 
 size_t deltanet_prefill_debug_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size) {
@@ -1154,6 +1241,51 @@ cudaError_t deltanet_test_withheld_load(const void* q, const void* k, const void
     L.ws = workspace; L.ws_bytes = workspace_bytes; L.stream = stream;
     L.force_kernel = kernel;
     L.withhold_v_chunk = withheld_chunk;
+    return gdn::launch(L);
+}
+
+// Long sequences cut into segments that run side by side (few sequences and heads leave most of
+// the GPU idle on the serial chunk recurrence). Three launches on `stream`: the state pass (every
+// segment from a zero state, giving A_j, and from the identity with zero v, giving Phi_j, in one
+// grid), the scan S_{j+1} = Phi_j S_j + A_j of entry states, and the output pass (every segment
+// from its entry state; only the last segment of each sequence writes its final state).
+cudaError_t deltanet_chunk_prefill_segmented(const void* q, const void* k, const void* v, const float* g,
+                                             const float* beta, const void* z, const void* norm_w, float eps,
+                                             void* out, const float* initial_state, float* final_state, int B,
+                                             int T, int HV, int HQK, int DK, int DV, int chunk_size, int segments,
+                                             void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if ((z == nullptr) != (norm_w == nullptr) || segments < 0) return cudaErrorInvalidValue;
+    if (DK != gdn::HD || DV != gdn::HD || chunk_size != gdn::CS || B < 0 || T < 0 || HV <= 0) return cudaErrorInvalidValue;
+    int nseg = 1, per = 1;
+    if (B > 0 && T > 0) gdn::resolve_segments(B, T, HV, segments, &nseg, &per);
+    if (nseg > 1 && !gdn::split_available()) nseg = 1;  // the segmented passes need the cluster-split kernel
+    if (nseg <= 1)  // one pass is the plain call
+        return z ? deltanet_chunk_prefill_gated(q, k, v, g, beta, z, norm_w, eps, out, initial_state, final_state, B, T,
+                                                HV, HQK, DK, DV, chunk_size, workspace, workspace_bytes, stream)
+                 : deltanet_chunk_prefill(q, k, v, g, beta, out, initial_state, final_state, B, T, HV, HQK, DK, DV,
+                                          chunk_size, workspace, workspace_bytes, stream, 0);
+    if (!workspace || workspace_bytes < gdn::segmented_bytes(B, HV, nseg)) return cudaErrorInvalidValue;
+    char* ws = static_cast<char*>(workspace);
+    void* zero = ws + gdn::WS_HEADER;
+    float* stt = reinterpret_cast<float*>(ws + gdn::WS_HEADER + gdn::SEG_ZERO_BYTES);  // [B nseg][2 HV][D][D]
+    float* entry = stt + (size_t)B * nseg * 2 * HV * gdn::HD * gdn::HD;                 // [B nseg][HV][D][D]
+    cudaError_t e = cudaMemsetAsync(zero, 0, gdn::SEG_ZERO_BYTES, stream);
+    if (e != cudaSuccess) return e;
+    gdn::Launch L = gdn::blank_launch();
+    L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.eps = eps;
+    L.nseq = B * nseg; L.B = B; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
+    L.max_nc = per;
+    L.ws = workspace; L.ws_bytes = workspace_bytes; L.stream = stream;
+    L.seg_chunks = per; L.seg_per_seq = nseg;
+    // state pass: A_j (zero entry, v) at heads [0, HV), Phi_j (identity entry, zero v) at [HV, 2 HV)
+    L.state_pass = 1; L.v0 = zero; L.sf = stt; L.out = nullptr;
+    e = gdn::launch(L);
+    if (e != cudaSuccess) return e;
+    e = gdn::launch_segment_scan(stt, initial_state, entry, B, HV, nseg, stream);
+    if (e != cudaSuccess) return e;
+    // output pass from the entry states; the last segment's final state is the sequence's
+    L.state_pass = 0; L.v0 = nullptr; L.z = z; L.w = norm_w; L.out = out;
+    L.s0 = entry; L.sf = final_state; L.sf_last_only = 1;
     return gdn::launch(L);
 }
 

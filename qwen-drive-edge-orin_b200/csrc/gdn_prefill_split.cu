@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         ptx::prefetch_tensormap(&p.tm_k);
         ptx::prefetch_tensormap(&p.tm_v);
         if (p.gated) ptx::prefetch_tensormap(&p.tm_z);
+        if ((int)blockIdx.y >= p.HV) ptx::prefetch_tensormap(&p.tm_v0);
     }
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -167,7 +168,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     const uint32_t rank = ptx::cluster_ctarank();
     const bool chain = (rank == CHAIN_RANK);
     const bool outcta = (rank == OUT_RANK);
-    const int h = blockIdx.y;
+    // state pass of a segmented call: y >= HV runs head y - HV from the identity with zero v
+    const bool phi_unit = (int)blockIdx.y >= p.HV;
+    const int h = phi_unit ? (int)blockIdx.y - p.HV : (int)blockIdx.y;
     const int seq = blockIdx.z;
     const int hq = h / (p.HV / p.HQK);
 
@@ -201,7 +204,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     ptx::grid_dependency_wait();
     ptx::grid_launch_dependents();
     int t_begin, len, bcoord;
-    if (p.cu_seqlens != nullptr) {
+    if (p.seg_chunks > 0) {  // segment seq % seg_per_seq of batch row seq / seg_per_seq
+        bcoord = seq / p.seg_per_seq;
+        t_begin = (seq - bcoord * p.seg_per_seq) * p.seg_chunks * CS;
+        len = min(p.seg_chunks * CS, p.T - t_begin);
+    } else if (p.cu_seqlens != nullptr) {
         t_begin = p.cu_seqlens[seq];
         len = p.cu_seqlens[seq + 1] - t_begin;
         bcoord = 0;
@@ -281,7 +288,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     uint32_t armed_a0 = 0, armed_a1 = 0, armed_b0 = 0, armed_b1 = 0, armed_o0 = 0, armed_o1 = 0;
     auto load_q = [&](int n) { load_tile(B_Q, C_QK, &p.tm_q, hq, n, armed_q); };
     auto load_k = [&](int n) { load_tile(B_K, C_QK + 8192, &p.tm_k, hq, n, armed_k); };
-    auto load_v = [&](int n) { load_tile(B_V, C_V, &p.tm_v, h, n, armed_v); };
+    auto load_v = [&](int n) { load_tile(B_V, C_V, phi_unit ? &p.tm_v0 : &p.tm_v, h, n, armed_v); };
     // L2 prefetch of a later chunk's tile (both 64-column boxes), so that its TMA load is an L2 hit
     auto prefetch_tile = [&](const CUtensorMap* map, int head, int n) {
         if (n * CS >= len) return;
@@ -336,7 +343,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 #pragma unroll
                 for (int j = 0; j < 64; ++j) {
                     const int dk = 64 * half + j;
-                    S[j] = (p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f;
+                    S[j] = phi_unit ? (dk == row ? 1.f : 0.f)
+                                    : ((p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f);
                 }
                 store_state_operand();
                 ptx::tmem_wait_st();
@@ -475,9 +483,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
             }
             if (!*abort_flag) {
-                const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
+                // final state: at (seq, blockIdx.y) (= (seq, h) outside a segmented state pass), or,
+                // in a segmented output pass, only the last segment's, at (batch row, h)
+                float* sfp = p.sf + ((size_t)seq * gridDim.y + blockIdx.y) * HD * HD;
+                if (p.sf_last_only)
+                    sfp = (seq % p.seg_per_seq == p.seg_per_seq - 1)
+                              ? p.sf + ((size_t)(seq / p.seg_per_seq) * p.HV + h) * HD * HD : nullptr;
+                if (sfp != nullptr) {
 #pragma unroll
-                for (int j = 0; j < 64; ++j) p.sf[sbase + (size_t)(64 * half + j) * HD + row] = S[j];
+                    for (int j = 0; j < 64; ++j) sfp[(size_t)(64 * half + j) * HD + row] = S[j];
+                }
             }
         } else if (!outcta) {
             // ---------------- prep CTA
@@ -723,7 +738,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         }
                     }
                 }
-                if (et < valid) {
+                if (et < valid && p.out != nullptr) {  // (a segmented state pass stores no output)
                     uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + et) * p.HV * HD + (size_t)h * HD);
 #pragma unroll
                     for (int m = 0; m < 4; ++m)
@@ -889,7 +904,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     const uint32_t ph = (uint32_t)(n & 1);
                     if (!wait_bar(B_VT, ph)) break;  // v^T T'^T has read the v tile
                     if (n + 1 < NC && n + 1 != p.withhold_v_chunk) load_v(n + 1);
-                    prefetch_tile(&p.tm_v, h, n + 2);
+                    if (!phi_unit) prefetch_tile(&p.tm_v, h, n + 2);
                     if (!wait_bar(B_VNR, ph) || *abort_flag) break;  // C12 read part A; decay factors copied
                     if (n + NSLOT < NC) arm_slot(B_FULLA, n, A_BYTES);
                     ptx::mbar_arrive_remote(prep_bar(B_EMPTYA, n));
@@ -1003,7 +1018,7 @@ bool split_available() {
     return split_prepare(dev) == cudaSuccess;
 }
 
-cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream) {
+cudaError_t launch_split(const Params& p, int nseq, int grid_heads, cudaStream_t stream) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -1011,7 +1026,7 @@ cudaError_t launch_split(const Params& p, int nseq, int HV, cudaStream_t stream)
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(split::CLUSTER, HV, nseq);
+    cfg.gridDim = dim3(split::CLUSTER, grid_heads, nseq);
     cfg.blockDim = dim3(split::NTHREADS, 1, 1);
     cfg.dynamicSmemBytes = split::SMEM_ALLOC;
     cfg.stream = stream;

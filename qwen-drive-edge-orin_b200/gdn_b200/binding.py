@@ -233,18 +233,14 @@ def chunk_prefill_varlen(q, k, v, g, beta, cu_seqlens, s0=None, z=None, w=None, 
     return [out, sf]
 
 
-# Default number of (segment, v-head) units per pass: the launcher runs up to 74 on the split
-# kernel (two waves of 37 four-CTA clusters on 148 SMs); at config 3's shape 18 segments per
-# sequence (72 units) ran faster than 9 (36 units, one wave): 1.73 vs 2.02 ms, the one-pass call 2.65.
-SEGMENT_UNITS = 74
-
-
 def segment_bounds(B: int, T: int, segments: int):
     """Cut each of B sequences of T tokens into at most ``segments`` runs of whole chunks.
 
     Returns (cu_seqlens over the B*T packed tokens as a list of ints, segments per sequence).
     Every segment but the last of a sequence is a multiple of the chunk length, so the
-    chunking inside a segment is the chunking of the whole sequence.
+    chunking inside a segment is the chunking of the whole sequence. This is the cut the
+    segmented kernels make (segment j of a sequence covers tokens [j p 64, min((j+1) p 64, T))
+    with p = ceil(chunks / segments) chunks per segment); the host-side form serves tests.
     """
     if B < 1 or T < 1 or segments < 1:
         raise ValueError("B, T and segments must be positive")
@@ -262,11 +258,10 @@ def segment_entry_states(Phi, A, s0=None):
     """Entry states of consecutive segments: S_0 = s0 (zeros if None), S_{j+1} = Phi_j S_j + A_j.
 
     Phi, A: [B, nseg, HV, d, d] (segment maps of each sequence, in order); s0: [B, HV, d, d].
-    Returns float32 [B, nseg, HV, d, d]. The scan runs in float64 (a few d x d GEMMs per
-    segment), so its rounding stays below the kernels' and does not depend on TF32 settings.
+    Returns float32 [B, nseg, HV, d, d]. The host-side form of the scan the segmented call runs
+    on the device (there in fp32, a block per 8 state columns); here in float64, for tests.
     """
     B, nseg, HV, d = A.shape[0], A.shape[1], A.shape[2], A.shape[3]
-    # [nseg, B*HV, d, d]: one batched GEMM-and-add per step (the scan is launch-bound)
     Phi = Phi.double().transpose(0, 1).reshape(nseg, B * HV, d, d)
     A = A.double().transpose(0, 1).reshape(nseg, B * HV, d, d)
     S = (torch.zeros_like(A[0]) if s0 is None
@@ -278,27 +273,6 @@ def segment_entry_states(Phi, A, s0=None):
     return torch.stack(states, dim=1).view(B, HV, nseg, d, d).transpose(1, 2).float().contiguous()
 
 
-_seg_lock = threading.Lock()
-_seg_cache: dict = {}
-
-
-def _segment_constants(dev, cu, N, HV, v_shape):
-    """Device constants of one segmentation, built once and reused: the int32 offsets, the
-    identity entry states and the zero v of the state-map pass (building them per call costs a
-    synchronous host-to-device copy and two allocations)."""
-    key = (dev, cu, N, HV, v_shape)
-    with _seg_lock:
-        c = _seg_cache.get(key)
-        if c is None:
-            if len(_seg_cache) > 16:
-                _seg_cache.clear()
-            cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
-            eye = torch.eye(HEAD_DIM, device=dev, dtype=torch.float32).expand(N, HV, HEAD_DIM, HEAD_DIM).contiguous()
-            c = (cu_t, eye, torch.zeros(v_shape, dtype=torch.bfloat16, device=dev))
-            _seg_cache[key] = c
-        return c
-
-
 def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: float = 1e-6,
                             segments: int | None = None):
     """Prefill of long sequences cut into segments that run in parallel: [o or y, final_state].
@@ -307,14 +281,13 @@ def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: floa
     given), for a few long sequences: one 65,536-token stream over 4 v-heads is a 1,024-step
     chain on 4 clusters of the split kernel, with most of the GPU idle. The state update of a
     chunk, S <- (e^{cL} I - K^T diag(e^{cL-c}) W) S + K^T diag(e^{cL-c}) U, is affine in S, so a
-    run of chunks maps its entry state as S_end = Phi S_start + A. With each sequence cut at
-    chunk boundaries into segments, three passes of the varlen prefill give the result:
-      1. every segment from a zero state: A (its final state);
-      2. every segment from the identity with v = 0: Phi (U = 0 there, so S_end = Phi I);
-      3. a scan S_{j+1} = Phi_j S_j + A_j (batched 128x128 GEMMs in float64, from s0), then
-         every segment from its S_j, which produces the output and the final state.
-    Each pass runs segments x heads units side by side. ``segments`` defaults to
-    SEGMENT_UNITS / (B * HV) per sequence; with one segment this is the plain call.
+    run of chunks maps its entry state as S_end = Phi S_start + A. ``deltanet_chunk_prefill_segmented``
+    cuts each sequence at chunk boundaries into segments and runs, on the current stream:
+      1. one grid with every segment from a zero state (A) and from the identity with v = 0 (Phi);
+      2. a device scan S_{j+1} = Phi_j S_j + A_j of the entry states, from s0;
+      3. every segment from its entry state, which produces the output and the final state.
+    ``segments`` (per sequence) defaults to the library's choice for this device and shape, which
+    is one pass when the heads alone fill the GPU.
     """
     B, T, HQK, HV = _check_inputs(q, k, v, g, beta)
     if (z is None) != (w is None):
@@ -322,24 +295,24 @@ def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: floa
     if z is not None and (z.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or not z.is_cuda or not w.is_cuda
                           or tuple(z.shape) != tuple(v.shape) or tuple(w.shape) != (HEAD_DIM,)):
         raise ValueError("z must be a bf16 CUDA tensor of v's shape and w a bf16 CUDA tensor [128]")
-    nseg = segments if segments is not None else max(1, SEGMENT_UNITS // (B * HV))
-    cu, per_seq = segment_bounds(B, T, nseg)
-    if per_seq == 1:
-        return chunk_prefill(q, k, v, g, beta, s0) if z is None else chunk_prefill_gated(q, k, v, g, beta, z, w, s0, eps)
-    dev = q.device
-    N = B * per_seq
-    pk = lambda t: t.contiguous().reshape(1, B * T, *t.shape[2:])  # noqa: E731  (packed, B = 1)
-    qp, kp, vp, gp, bp = (pk(t) for t in (q, k, v, g, beta))
-    cu_t, eye, v_zero = _segment_constants(dev, tuple(cu), N, HV, tuple(vp.shape))
-    _, A = chunk_prefill_varlen(qp, kp, vp, gp, bp, cu_t)
-    _, Phi = chunk_prefill_varlen(qp, kp, v_zero, gp, bp, cu_t, s0=eye)
-    s0 = None if s0 is None else _state(s0, (B, HV, HEAD_DIM, HEAD_DIM), dev)
-    starts = segment_entry_states(Phi.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM),
-                                  A.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM), s0)
-    zp = None if z is None else pk(z)
-    out, sf = chunk_prefill_varlen(qp, kp, vp, gp, bp, cu_t, s0=starts.view(N, HV, HEAD_DIM, HEAD_DIM), z=zp, w=w,
-                                   eps=eps)
-    return [out.view(B, T, HV, HEAD_DIM), sf.view(B, per_seq, HV, HEAD_DIM, HEAD_DIM)[:, -1].contiguous()]
+    dev = _same_device(q, z, w)
+    seg = 0 if segments is None else int(segments)
+    if seg < 0:
+        raise ValueError("segments must be >= 0 (0: the library's choice)")
+    lib = load_library()
+    q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
+    if z is not None:
+        z, w = z.contiguous(), w.contiguous()
+    out = torch.empty_like(v)
+    sf = torch.empty(B, HV, HEAD_DIM, HEAD_DIM, device=dev, dtype=torch.float32)
+    s0 = _state(s0, (B, HV, HEAD_DIM, HEAD_DIM), dev)
+    with torch.cuda.device(dev):
+        ws = _workspace(dev, int(lib.deltanet_segmented_workspace_size(B, T, HV, HEAD_DIM, HEAD_DIM, CHUNK, seg)))
+        code = lib.deltanet_chunk_prefill_segmented(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(z), _ptr(w),
+                                                    float(eps), _ptr(out), _ptr(s0), _ptr(sf), B, T, HV, HQK,
+                                                    HEAD_DIM, HEAD_DIM, CHUNK, seg, _ptr(ws), ws.numel(), _stream())
+    _check(code, "deltanet_chunk_prefill_segmented")
+    return [out, sf]
 
 
 def gated_rmsnorm(o, z, w, eps: float = 1e-6):

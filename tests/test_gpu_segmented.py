@@ -1,9 +1,10 @@
-"""The segmented prefill (segments of a long sequence run side by side, their entry states
-from a scan of the segments' affine state maps) against the plain one-pass prefill, on B200.
+"""The segmented prefill (deltanet_chunk_prefill_segmented: segments of a long sequence run
+side by side, their entry states from a device scan of the segments' affine state maps)
+against the plain one-pass prefill, on B200.
 
 Both paths run the same kernels over the same chunks; they differ only in how the state
-reaches each segment (the scan in float64 instead of the chunk recurrence in fp32), so they
-agree far inside the parity bars that tie the plain path to the oracle.
+reaches each segment (the scan of the maps instead of the chunk recurrence), so they agree
+far inside the parity bars that tie the plain path to the oracle.
 """
 from __future__ import annotations
 
@@ -78,4 +79,50 @@ def test_one_segment_is_the_plain_call():
     inp = make_inputs(1, 700, 2, 4, seed=12)
     o_ref, sf_ref = _run("plain", inp, False)
     o, sf = _run("segmented", inp, False, segments=1)
+    assert np.array_equal(o, o_ref) and np.array_equal(sf, sf_ref)
+
+
+def _timed(fn, reps=5):
+    import statistics
+    for _ in range(2):
+        fn()
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def test_config3_shard_library_choice_against_one_pass():
+    """One rank's shard of BASELINE config 3 (B=1, S=65536, 4 v-heads, 2 qk-heads, zero initial
+    state, fused norm) with the library's segment choice against the one-pass call; both timed
+    (CUDA events, median of 5 after 2 warm-ups, through the binding)."""
+    import warnings
+    inp = make_inputs(1, 65536, 2, 4, seed=3, with_s0=False)
+    q, k, v, z, w = _dev(inp.q), _dev(inp.k), _dev(inp.v), _dev(inp.z), _dev(inp.w)
+    g, b = _dev(inp.g, torch.float32), _dev(inp.beta, torch.float32)
+    lib = gdn_b200.load_library()
+    nbytes = lib.deltanet_segmented_workspace_size(1, 65536, 4, 128, 128, 64, 0)
+    assert nbytes > 256, "the library should cut a 4-head 65,536-token stream into segments"
+    y1, sf1 = gdn_b200.chunk_prefill_gated(q, k, v, g, b, z, w)
+    y, sf = gdn_b200.chunk_prefill_segmented(q, k, v, g, b, z=z, w=w)
+    torch.cuda.synchronize()
+    y1, sf1, yh, sfh = (t.float().cpu().numpy() for t in (y1, sf1, y, sf))
+    assert max_rel(yh, y1) < Y_MAX_REL and tensor_l2_rel(sfh, sf1) < 1e-4
+    t_one = _timed(lambda: gdn_b200.chunk_prefill_gated(q, k, v, g, b, z, w))
+    t_seg = _timed(lambda: gdn_b200.chunk_prefill_segmented(q, k, v, g, b, z=z, w=w))
+    nseg = (nbytes - 256 - 16384) // (3 * 4 * 128 * 128 * 4)
+    warnings.warn(f"config-3 shard (S=65536, 4 v-heads): one pass {t_one:.3f} ms, segmented "
+                  f"({nseg} segments) {t_seg:.3f} ms")
+
+
+def test_full_gpu_takes_one_pass():
+    """With 32 heads the GPU is full: the library's choice is one pass, the plain call's result."""
+    inp = make_inputs(1, 700, 16, 32, seed=14, with_s0=True)
+    o_ref, sf_ref = _run("plain", inp, True)
+    o, sf = _run("segmented", inp, True)
     assert np.array_equal(o, o_ref) and np.array_equal(sf, sf_ref)
