@@ -423,6 +423,8 @@ def main():
     ap.add_argument("--windows", type=int, default=10, help="repeats of the K-step window (spread)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 block of a default run")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="diagnostic: run rank 0's shard of an N-GPU job on this one GPU (per-GPU figures)")
     ap.add_argument("--graph-launches", type=int, default=20,
                     help="launches captured in one CUDA graph for the graph timing (0: skip)")
     args = ap.parse_args()
@@ -448,7 +450,12 @@ def main():
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
-    wl = Workload(args.config, rank, world, device)
+    if args.shard_of > 1 and world == 1:  # one rank's share of an N-GPU job, alone on this GPU
+        wl = Workload(args.config, 0, args.shard_of, device)
+        wl.job_tokens //= (args.shard_of if wl.scaling == "weak" else 1)
+        wl.parallelism = f"diagnostic: rank 0's shard of a {args.shard_of}-GPU job, alone on one GPU; " + wl.parallelism
+    else:
+        wl = Workload(args.config, rank, world, device)
     # inputs: rotate through enough copies that each step's working set was evicted from L2
     step_bytes = wl.step_bytes
     n_sets = max(1, math.ceil(3 * L2_BYTES / step_bytes)) if step_bytes < 3 * L2_BYTES else 1

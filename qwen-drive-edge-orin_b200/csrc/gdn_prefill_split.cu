@@ -148,6 +148,9 @@ constexpr uint32_t T_VN_HI = 0, T_VN_LO = 32, T_VP_HI = 64, T_VP_LO = 96, T_O = 
 // prep: [0,64) P1; [128,256) P3 [T''_hi | T''_lo] parts of W^T
 constexpr uint32_t T_P = 0, T_W = 128;
 
+// kSeg: the instantiation for the passes of a segmented call (segment indexing, the state
+// pass's identity runs, last-segment final states); the plain instantiation carries none of it.
+template <bool kSeg>
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __grid_constant__ Params p) {
     // the tensor maps are kernel parameters, not data of the previous launch: fetch them while it ends
     if (threadIdx.x == 0) {
@@ -155,7 +158,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         ptx::prefetch_tensormap(&p.tm_k);
         ptx::prefetch_tensormap(&p.tm_v);
         if (p.gated) ptx::prefetch_tensormap(&p.tm_z);
-        if ((int)blockIdx.y >= p.HV) ptx::prefetch_tensormap(&p.tm_v0);
+        if (kSeg && (int)blockIdx.y >= p.HV) ptx::prefetch_tensormap(&p.tm_v0);
     }
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     const bool chain = (rank == CHAIN_RANK);
     const bool outcta = (rank == OUT_RANK);
     // state pass of a segmented call: y >= HV runs head y - HV from the identity with zero v
-    const bool phi_unit = (int)blockIdx.y >= p.HV;
+    const bool phi_unit = kSeg && (int)blockIdx.y >= p.HV;
     const int h = phi_unit ? (int)blockIdx.y - p.HV : (int)blockIdx.y;
     const int seq = blockIdx.z;
     const int hq = h / (p.HV / p.HQK);
@@ -204,7 +207,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     ptx::grid_dependency_wait();
     ptx::grid_launch_dependents();
     int t_begin, len, bcoord;
-    if (p.seg_chunks > 0) {  // segment seq % seg_per_seq of batch row seq / seg_per_seq
+    if (kSeg) {  // segment seq % seg_per_seq of batch row seq / seg_per_seq
         bcoord = seq / p.seg_per_seq;
         t_begin = (seq - bcoord * p.seg_per_seq) * p.seg_chunks * CS;
         len = min(p.seg_chunks * CS, p.T - t_begin);
@@ -486,7 +489,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 // final state: at (seq, blockIdx.y) (= (seq, h) outside a segmented state pass), or,
                 // in a segmented output pass, only the last segment's, at (batch row, h)
                 float* sfp = p.sf + ((size_t)seq * gridDim.y + blockIdx.y) * HD * HD;
-                if (p.sf_last_only)
+                if (kSeg && p.sf_last_only)
                     sfp = (seq % p.seg_per_seq == p.seg_per_seq - 1)
                               ? p.sf + ((size_t)(seq / p.seg_per_seq) * p.HV + h) * HD * HD : nullptr;
                 if (sfp != nullptr) {
@@ -738,7 +741,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         }
                     }
                 }
-                if (et < valid && p.out != nullptr) {  // (a segmented state pass stores no output)
+                if (et < valid && (!kSeg || p.out != nullptr)) {  // (a segmented state pass stores no output)
                     uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(tok0 + et) * p.HV * HD + (size_t)h * HD);
 #pragma unroll
                     for (int m = 0; m < 4; ++m)
@@ -997,17 +1000,19 @@ static cudaError_t split_prepare(int dev) {
     static int state[64] = {};  // 0 unchecked, 1 ready, 2 unusable
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (state[dev] == 0) {
-        cudaFuncAttributes fa;
-        cudaError_t e = cudaFuncGetAttributes(&fa, split::gdn_prefill_split_kernel);
-        if (e != cudaSuccess) return e;
-        if (fa.numRegs != split::LAUNCH_REGS) {
-            state[dev] = 2;
-        } else {
-            e = cudaFuncSetAttribute(split::gdn_prefill_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)split::SMEM_ALLOC);
+        int ok = 1;
+        for (auto fn : {split::gdn_prefill_split_kernel<false>, split::gdn_prefill_split_kernel<true>}) {
+            cudaFuncAttributes fa;
+            cudaError_t e = cudaFuncGetAttributes(&fa, fn);
             if (e != cudaSuccess) return e;
-            state[dev] = 1;
+            if (fa.numRegs != split::LAUNCH_REGS) {
+                ok = 0;
+                break;
+            }
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::SMEM_ALLOC);
+            if (e != cudaSuccess) return e;
         }
+        state[dev] = ok ? 1 : 2;
     }
     return state[dev] == 1 ? cudaSuccess : cudaErrorNotSupported;
 }
@@ -1040,7 +1045,8 @@ cudaError_t launch_split(const Params& p, int nseq, int grid_heads, cudaStream_t
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    e = cudaLaunchKernelEx(&cfg, split::gdn_prefill_split_kernel, p);
+    e = p.seg_chunks > 0 ? cudaLaunchKernelEx(&cfg, split::gdn_prefill_split_kernel<true>, p)
+                         : cudaLaunchKernelEx(&cfg, split::gdn_prefill_split_kernel<false>, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
