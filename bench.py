@@ -93,14 +93,15 @@ def load_peaks():
 
 
 def load_traffic(config):
-    """(per-launch DRAM bytes, kernel name) of the config's prefill kernel from the committed
-    ncu summary, or (None, None)."""
+    """(per-launch memory traffic in bytes, kernel name) of the config's prefill kernel from the
+    committed ncu summary, or (None, None): DRAM reads plus the writes the SMs send to L2 (the
+    outputs are still in L2 when a launch ends, so DRAM write counters miss them)."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None, None
     d = json.loads(p.read_text())
     v = d.get(f"config{config}")
-    return (None, None) if v is None else (float(v["dram_bytes_per_launch"]), v.get("kernel"))
+    return (None, None) if v is None else (float(v["traffic_bytes_per_launch"]), v.get("kernel"))
 
 
 # ----------------------------------------------------------------- clocks
@@ -270,7 +271,7 @@ class Workload:
         return gdn_b200.chunk_prefill_gated(d["q"], d["k"], d["v"], d["g"], d["beta"], d["z"], d["w"], d.get("s0"))
 
 
-GATE_CYCLES = 4_000_000  # ~2 ms of device spin ahead of a timed window
+GATE_CYCLES = 1_000_000  # ~0.5 ms of device spin ahead of a timed window (the host enqueues ~30 calls meanwhile)
 
 
 def time_window(wl, sets, outs, stream, steps, start=0):
@@ -533,7 +534,8 @@ def main():
     traffic, traffic_kernel = load_traffic(args.config)
     override = os.environ.get("GDN_B200_KERNEL", "auto")
     if override in ("fused", "split"):  # the launcher's kernel choice was overridden
-        launched = "gdn::split::gdn_prefill_split_kernel" if override == "split" else "gdn::gdn_prefill_kernel"
+        launched = ("gdn::split::gdn_prefill_split_kernel<false>" if override == "split"
+                    else "gdn::gdn_prefill_kernel<false, false>")
         if traffic_kernel != launched:  # the committed traffic figure is another kernel's
             traffic, traffic_kernel = None, launched
     roofline = {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_gbs, "unit": "GB/s",

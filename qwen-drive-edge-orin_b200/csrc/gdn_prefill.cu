@@ -864,6 +864,7 @@ cudaError_t launch_split(const Params& p, int nseq, int grid_heads, cudaStream_t
 cudaError_t launch_segment_scan(const float* stt, const float* s0, float* entry, int B, int HV, int nseg,
                                 cudaStream_t stream);  // gdn_segment_scan.cu
 int split_cluster_ctas();
+int split_clusters_per_wave();
 bool split_available();
 
 // Kernel choice: the cluster-split kernel when the (sequence, head) clusters run
@@ -1051,22 +1052,25 @@ static cudaError_t noalloc_scratch(void** out) {
 // Long sequences in segments (deltanet_chunk_prefill_segmented).
 constexpr size_t SEG_ZERO_BYTES = (size_t)CS * HD * 2;  // one zero bf16 tile [64 tok][128]: the identity runs' v
 
-// Segments per sequence for B sequences of NC chunks and HV v-heads on `sms` SMs, from a wave
-// model of the cluster-split kernel (4-CTA clusters, sms / 4 per wave, one chunk period per
-// chunk): the segmented call costs (waves of 2 U s units + waves of U s units) * ceil(NC / s)
-// chunk periods, U = B HV (state pass, then output pass; the scan is small), against
-// waves(U) * NC for one pass. Returns the cheapest s (1: one pass), the smaller on ties.
-static int auto_segments(int B, int HV, int NC, int sms) {
-    const long long wave = sms / split_cluster_ctas(), U = (long long)B * HV;
+// Segments per sequence for B sequences of NC chunks and HV v-heads, `wave` clusters of the
+// cluster-split kernel at once, from a wave model: a wave of clusters costs its chunks' periods
+// plus about WAVE_OVERHEAD periods of start-up and drain (the first chunk's preparation and
+// shipment before the chain can start, the last chunk's output after it), so the segmented call
+// costs (waves of 2 U s units + waves of U s units) * (ceil(NC / s) + overhead), U = B HV
+// (state pass, then output pass; the scan is small), against waves(U) * (NC + overhead) for
+// one pass. Returns the cheapest s (1: one pass), the smaller on ties.
+constexpr int WAVE_OVERHEAD = 5;
+static int auto_segments(int B, int HV, int NC, int wave) {
+    const long long U = (long long)B * HV;
     if (wave <= 0 || NC <= 1) return 1;
     auto waves = [&](long long units) { return (units + wave - 1) / wave; };
-    long long best_cost = waves(U) * NC;
+    long long best_cost = waves(U) * (NC + WAVE_OVERHEAD);
     int best = 1;
     for (int s = 2; s <= NC && s <= 256; ++s) {
         const long long per = (NC + s - 1) / s;
         const long long eff = (NC + per - 1) / per;  // segments actually made with `per` chunks each
         if (eff != s) continue;
-        const long long cost = (waves(2 * U * s) + waves(U * s)) * per;
+        const long long cost = (waves(2 * U * s) + waves(U * s)) * (per + WAVE_OVERHEAD);
         if (cost < best_cost) {
             best_cost = cost;
             best = s;
@@ -1081,11 +1085,14 @@ static void resolve_segments(int B, int T, int HV, int segments, int* nseg, int*
     const int NC = (T + CS - 1) / CS;
     int s = segments;
     if (s <= 0) {
-        int dev = 0, sms = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-            sms = 0;
-        s = auto_segments(B, HV, NC, sms);
+        int wave = split_clusters_per_wave();
+        if (wave <= 0) {  // no occupancy answer: SMs / cluster size
+            int dev = 0, sms = 0;
+            if (cudaGetDevice(&dev) == cudaSuccess &&
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+                wave = sms / split_cluster_ctas();
+        }
+        s = auto_segments(B, HV, NC, wave);
     }
     if (NC <= 1 || s <= 1) {
         *nseg = 1;

@@ -1053,4 +1053,35 @@ cudaError_t launch_split(const Params& p, int nseq, int grid_heads, cudaStream_t
 
 int split_cluster_ctas() { return split::CLUSTER; }
 
+// Clusters of the split kernel that fit the current device at once (one wave), from the
+// occupancy API (clusters must fit inside a GPC, so this can be below SMs / cluster size;
+// 32 on B200 against 148 / 4 = 37); 0 if the kernel cannot run. Cached per device.
+int split_clusters_per_wave() {
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cache[dev] == 0) {
+        if (split_prepare(dev) != cudaSuccess) return 0;
+        cudaLaunchConfig_t cfg;
+        memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(split::CLUSTER, 1, 1);
+        cfg.blockDim = dim3(split::NTHREADS, 1, 1);
+        cfg.dynamicSmemBytes = split::SMEM_ALLOC;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = split::CLUSTER;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, split::gdn_prefill_split_kernel<false>, &cfg) != cudaSuccess) {
+            cudaGetLastError();  // clear it: the caller falls back to SMs / cluster size
+            n = -1;
+        }
+        cache[dev] = n;
+    }
+    return cache[dev] > 0 ? cache[dev] : 0;
+}
+
 }  // namespace gdn
