@@ -651,8 +651,8 @@ def run_reference(args, cfg, world, rank, warmup):
     """The reference's CPU implementation of the path, timed on this host's cores (rank 0 only)."""
     if rank != 0:
         return
-    B, T, HQK, HV = cfg["B"], cfg["T"], cfg["HQK"], cfg["HV"]
-    sample, sb = cpu_sample_inputs(cfg)
+    B, HQK, HV = cfg["B"], cfg["HQK"], cfg["HV"]
+    sample, sb, T = cpu_sample_inputs(cfg)  # T: the sample's tokens per sequence
     from oracle.torch_reference import reference_gated_prefill
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
@@ -670,7 +670,7 @@ def run_reference(args, cfg, world, rank, warmup):
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
             "warmup": warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded, BASELINE distributions)",
-            "config": {"workload": cfg["desc"], "global_batch": B, "seq_len": T, "parallelism": "host CPU"},
+            "config": {"workload": cfg["desc"], "global_batch": B, "seq_len": cfg["T"], "parallelism": "host CPU"},
             "impl": "reference",
             "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads, "kind": "reference",
                              "sample": desc},

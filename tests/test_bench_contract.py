@@ -55,3 +55,20 @@ def test_committed_traffic_and_peaks_are_readable():
         d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
         assert kind == "measured" and hbm == float(d["hbm_gbs"])
     assert hbm > 1000 and tf_burst > 100
+
+
+def test_reference_arm_prints_one_json_line():
+    """``bench.py --impl reference`` (the driver's reference arm) runs the reference's CPU
+    implementation on this host and prints one JSON line with the contract's keys."""
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "1"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["value"] > 0 and d["higher_is_better"]
+    assert d["cpu_baseline"]["kind"] == "reference" and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["config"]["workload"] == bench.CONFIGS[1]["desc"] and d["config"]["seq_len"] == 1141
