@@ -82,8 +82,8 @@ constexpr uint32_t MISC_BETA = 256; // beta     [64]
 constexpr uint32_t MISC_EC = 512;   // e^c      [64]
 constexpr uint32_t MISC_ED = 768;   // e^{cL-c} [64]
 constexpr uint32_t MISC_BAR = 1024; // NBAR mbarriers
-constexpr uint32_t MISC_TMEM = 1088;
-constexpr uint32_t MISC_FLAG = 1092;
+constexpr uint32_t MISC_TMEM = 1104;
+constexpr uint32_t MISC_FLAG = 1108;
 constexpr uint32_t MISC_W = 1152;   // norm weight [128] f32
 constexpr uint32_t MISC_BYTES = 1664;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
@@ -106,8 +106,11 @@ constexpr uint32_t TM_SA_HI = 384; // S^T bf16 pairs, A operand of C12 / C3 (64)
 constexpr uint32_t TM_SA_LO = 448;
 
 // Barrier slots: TMA tiles; MMA commit groups (BAR_MMA: every group but the two below, which
-// let the state update start while the output products still run: BAR_DS = dS, BAR_O1 = S^T q^T).
-enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4, BAR_DS = 5, BAR_O1 = 6, NBAR = 7 };
+// let the state update start while the output products still run: BAR_DS = dS, BAR_O1 = S^T q^T,
+// BAR_O2 = v_new^T M^T, issued by thread 32 once thread 0 has issued dS and arrived on BAR_DSI).
+enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4, BAR_DS = 5, BAR_O1 = 6, BAR_O2 = 7, BAR_DSI = 8,
+       NBAR = 9 };
+static_assert(MISC_BAR + 8 * NBAR <= MISC_TMEM, "barriers overlap the TMEM address word");
 
 
 // Debug record layout (floats) per (seq, head, chunk).
@@ -212,7 +215,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                    : (kPrestage ? __half2float(reinterpret_cast<const __half*>(p.w)[tid]) : __bfloat162float(p.w[tid]));
 
     // ---- TMA issue helpers (thread 0) ----
-    uint32_t issued[NBAR] = {0, 0, 0, 0, 0, 0, 0}, consumed[NBAR] = {0, 0, 0, 0, 0, 0, 0};
+    uint32_t issued[NBAR] = {}, consumed[NBAR] = {};
     auto load_q = [&](int n) {
         ++issued[BAR_Q];
         ptx::mbar_arrive_expect_tx(bar(BAR_Q), 16384);
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         load_k(0);
         if (p.withhold_v_chunk != 0) load_v(0);
     }
-    if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z is consumed by warps 4-7 (gate precompute)
+    if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z feeds the gate product (while C12 runs)
     // Gate inputs of the next chunk are prefetched into warp 1's registers (lane l: tokens 2l,
     // 2l+1) as raw values: loaded unconditionally (positions past the sequence end are clamped
     // to its last token), transformed and masked only when that chunk is processed, so that
@@ -444,44 +447,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::tc_fence_before();
         __syncthreads();
 
-        // ---- T = (I + L)^-1 (fp32, CUDA cores); meanwhile warps 4-7 form gate = w * silu(z) ----
-        auto gate_work = [&](int phase) {
-            if (!p.gated) return;
-            if (phase == 0) wait_bar(BAR_Z, ph);
-            const int tg = tid - 128;
-            const int r0 = (phase == 0) ? 0 : (phase == 1 ? 32 : 48), nr = (phase == 0) ? 32 : 16;
-            for (int u = tg; u < nr * 16; u += 128) {
-                const int r = r0 + (u >> 4), zc = u & 15;
-                uint32_t w4[4];
-                ld_shared_v4(sb + OFF_Z + sw_chunk(r, zc, 64), w4[0], w4[1], w4[2], w4[3]);
-                float gv[8];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float z0, z1;
-                    if (kPrestage) {
-                        const __half2 z2 = *reinterpret_cast<const __half2*>(&w4[e]);
-                        z0 = __low2float(z2), z1 = __high2float(z2);
-                    } else {
-                        const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
-                        z0 = __low2float(z2), z1 = __high2float(z2);
-                    }
-                    gv[2 * e] = w_s[8 * zc + 2 * e] * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
-                    gv[2 * e + 1] = w_s[8 * zc + 2 * e + 1] * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
-                }
-                *reinterpret_cast<float4*>(smem + OFF_GATE + gate_chunk(r, 2 * zc)) =
-                    make_float4(gv[0], gv[1], gv[2], gv[3]);
-                *reinterpret_cast<float4*>(smem + OFF_GATE + gate_chunk(r, 2 * zc + 1)) =
-                    make_float4(gv[4], gv[5], gv[6], gv[7]);
-            }
-            if (phase == 2) {
-                asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 4-7 are done with the z tile
-                if (tid == 128 && n + 1 < NC && !*abort_flag) {
-                    ptx::fence_proxy_async_smem();
-                    load_z(n + 1);
-                }
-            }
-        };
-        invert_unit_lower<true>(Ls, X, tid, gate_work, [] { __syncthreads(); });
+        // ---- T = (I + L)^-1 (fp32, CUDA cores) ----
+        invert_unit_lower<true>(Ls, X, tid, [](int) {}, [] { __syncthreads(); });
         if (rec) {
             for (int e = tid; e < CS * CS; e += NTHREADS) rec[DBG_T + e] = Ls[(e >> 6) * LSTRIDE + (e & 63)];
             if (tid < CS) rec[DBG_C + tid] = c_s[tid];
@@ -587,6 +554,35 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             }
             commit();
         }
+        // ---- gate = w * silu(z) for this chunk's epilogue, by every thread while C12 runs (the
+        //      SFU-bound product slowed the triangular inverse by ~1.6 K cycles when warps 4-7 ran
+        //      it alongside; here the warps would otherwise only wait for the MMAs) ----
+        if (p.gated) {
+            wait_bar(BAR_Z, ph);
+            for (int u = tid; u < CS * 16; u += NTHREADS) {
+                const int r = u >> 4, zc = u & 15;
+                uint32_t w4[4];
+                ld_shared_v4(sb + OFF_Z + sw_chunk(r, zc, 64), w4[0], w4[1], w4[2], w4[3]);
+                float gv[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float z0, z1;
+                    if (kPrestage) {
+                        const __half2 z2 = *reinterpret_cast<const __half2*>(&w4[e]);
+                        z0 = __low2float(z2), z1 = __high2float(z2);
+                    } else {
+                        const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
+                        z0 = __low2float(z2), z1 = __high2float(z2);
+                    }
+                    gv[2 * e] = w_s[8 * zc + 2 * e] * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
+                    gv[2 * e + 1] = w_s[8 * zc + 2 * e + 1] * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
+                }
+                *reinterpret_cast<float4*>(smem + OFF_GATE + gate_chunk(r, 2 * zc)) =
+                    make_float4(gv[0], gv[1], gv[2], gv[3]);
+                *reinterpret_cast<float4*>(smem + OFF_GATE + gate_chunk(r, 2 * zc + 1)) =
+                    make_float4(gv[4], gv[5], gv[6], gv[7]);
+            }
+        }
         wait_mma();
         if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk && !*abort_flag) load_v(n + 1);  // v tile consumed
         {   // v_new^T (fp32, cols TM_C12) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
@@ -624,6 +620,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         }
         ptx::tc_fence_before();
         __syncthreads();
+        if (tid == 128 && p.gated && n + 1 < NC && !*abort_flag) {  // every thread is done with the z tile
+            ptx::fence_proxy_async_smem();
+            load_z(n + 1);
+        }
         if (*abort_flag) break;
 
         // ---- C4: dS^T = v_new'^T K ; C3: o1^T = S^T q^T, o2^T = v_new^T M^T. dS first, each group
@@ -640,6 +640,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
             }
             commit_to(BAR_DS);
+            ptx::mbar_arrive(bar(BAR_DSI));  // dS is in the tensor pipe ahead of the output products
 #pragma unroll
             for (int part = 0; part < 2; ++part) {
                 const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
@@ -650,7 +651,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
             }
             commit_to(BAR_O1);
-            // (VN_hi, M_hi), (VN_lo, M_hi), (VN_hi, M_lo)
+        } else if (tid == 32) {
+            // v_new^T M^T on a second issuing thread: an MMA issue occupies its thread for about the
+            // instruction's execution time, and on thread 0 alone the 36 MMAs held warp 0 back from
+            // its state update. (VN_hi, M_hi), (VN_lo, M_hi), (VN_hi, M_lo)
+            wait_bar(BAR_DSI, consumed[BAR_DSI] & 1u);
+            ptx::tc_fence_after();
+            if (!*abort_flag) {  // (after a failed wait nothing more is issued; the consumers' waits run out)
 #pragma unroll
             for (int term = 0; term < 3; ++term) {
                 const uint32_t va = (term == 1) ? TM_VN_LO : TM_VN_HI;
@@ -661,7 +668,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                     ptx::mma_bf16_ts(tmem + TM_O2, tmem + va + 8 * s, b, ID_O, (term | s) > 0);
                 }
             }
-            commit();
+            commit_to(BAR_O2);
+            }
         }
         wait_bar(BAR_DS, consumed[BAR_DS] & 1u);
         ptx::tc_fence_after();
@@ -689,7 +697,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             load_k(n + 1);
         }
         store_state_operand();  // new S^T hi/lo for the next chunk's C12 / C3, while v_new^T M^T runs
-        wait_mma();             // v_new^T M^T done
+        wait_bar(BAR_O2, consumed[BAR_O2] & 1u);  // v_new^T M^T done
+        ptx::tc_fence_after();
 
         // ---- o = scale e^c o1 + o2, rounded to bf16, staged [tok][dv] in the (free) L region ----
         {
@@ -786,7 +795,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     }
     // Abort path: wait (bounded) for this CTA's own TMA copies and MMAs still
     // in flight before its shared memory and TMEM are released.
-    if (*abort_flag && (tid == 0 || tid == 128)) {
+    if (*abort_flag && (tid == 0 || tid == 32 || tid == 128)) {
 #pragma unroll
         for (int i = 0; i < NBAR; ++i)
             while (consumed[i] < issued[i]) {
