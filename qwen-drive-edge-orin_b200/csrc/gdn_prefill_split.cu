@@ -106,7 +106,8 @@ constexpr uint32_t P_MISC = P_GATE + 2 * GSLOT;
 constexpr uint32_t U_OSLOT = 0;                  // 2 o^T slots (chunk parity), filled by the chain CTA
 constexpr uint32_t U_Z = 2 * O_BYTES;            // 2 z tiles (chunk parity)
 constexpr uint32_t U_OT = U_Z + 2 * O_BYTES;     // o [64 tok][128 dv] (two 64-row panels), transposed here
-constexpr uint32_t U_MISC = U_OT + O_BYTES;
+constexpr uint32_t U_GATE = U_OT + O_BYTES;      // w * silu(z) fp32 [64 tok][128 dv], 16-byte chunks swizzled
+constexpr uint32_t U_MISC = U_GATE + 2 * O_BYTES;
 // ---- misc (all roles; the chain keeps e^c of chunks with even / odd index at M_C, 128 floats)
 constexpr uint32_t M_C = 0, M_W = 512, M_BAR = 1024, M_TMEM = 1280, M_FLAG = 1284, M_DONE = 1288,
                    M_BYTES = 1408;
@@ -659,7 +660,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             // ---------------- output CTA: gated-RMSNorm epilogue of every chunk (4 threads per
             // token, 16-byte chunks {eq, eq+4, eq+8, eq+12}); o arrives from the chain CTA
             const int et = tid >> 2, eq = tid & 3;
-            if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;  // read after the first o slot lands
+            if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;
+            csync();  // w_s visible to every thread (the first gate tile reads it)
             auto load_zt = [&](int n) {
                 if (n & 1) load_tile(B_ZT + 1, U_Z + O_BYTES, &p.tm_z, h, n, armed_z1);
                 else load_tile(B_ZT, U_Z, &p.tm_z, h, n, armed_z0);
@@ -673,6 +675,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 const uint32_t par = (uint32_t)((n >> 1) & 1);
                 const uint32_t oslot = U_OSLOT + (uint32_t)(n & 1) * O_BYTES;
                 const uint32_t zt = U_Z + (uint32_t)(n & 1) * O_BYTES;
+                if (p.gated) {
+                    // gate = w * silu(z) of chunk n, formed while this CTA waits for o(n) from the chain (the
+                    // SFU-bound part of the epilogue is then off the last chunk's path); then z(n + 2) loads
+                    wait_bar(B_ZT + (n & 1), par);
+                    for (int u = tid; u < CS * 16; u += NCOMPUTE) {
+                        const int r = u >> 4, zc = u & 15;
+                        uint32_t w4[4];
+                        ld_shared_v4(sb + zt + sw_chunk(r, zc, 64), w4[0], w4[1], w4[2], w4[3]);
+                        float gv[8];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
+                            const float z0 = __low2float(z2), z1 = __high2float(z2);
+                            gv[2 * e] = w_s[8 * zc + 2 * e] * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
+                            gv[2 * e + 1] = w_s[8 * zc + 2 * e + 1] * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
+                        }
+                        *reinterpret_cast<float4*>(smem + U_GATE + gate_chunk(r, 2 * zc)) =
+                            make_float4(gv[0], gv[1], gv[2], gv[3]);
+                        *reinterpret_cast<float4*>(smem + U_GATE + gate_chunk(r, 2 * zc + 1)) =
+                            make_float4(gv[4], gv[5], gv[6], gv[7]);
+                    }
+                    csync();  // gate tile written; z tile read
+                    if (tid == 0 && !*abort_flag && n + 2 < NC) {  // this parity's z tile takes chunk n + 2
+                        ptx::fence_proxy_async_smem();
+                        load_zt(n + 2);
+                        prefetch_tile(&p.tm_z, h, n + 3);
+                    }
+                }
                 wait_bar(B_FULLO + (n & 1), par);
                 {   // o^T -> o: thread (dv, token half) reads four 16-byte chunks of row dv
                     const int dv = tid >> 1, th = tid & 1;
@@ -723,21 +753,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
                     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
                     const float rstd = rsqrtf(ss * (1.f / (float)HD) + p.eps);
-                    wait_bar(B_ZT + (n & 1), par);
 #pragma unroll
                     for (int m = 0; m < 4; ++m) {
                         const int c = eq + 4 * m;
-                        uint32_t w4[4];
-                        ld_shared_v4(sb + zt + sw_chunk(et, c, 64), w4[0], w4[1], w4[2], w4[3]);
+                        const float4 g0 = *reinterpret_cast<const float4*>(smem + U_GATE + gate_chunk(et, 2 * c));
+                        const float4 g1 = *reinterpret_cast<const float4*>(smem + U_GATE + gate_chunk(et, 2 * c + 1));
+                        const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
-                            const int j = 8 * m + 2 * u, dv = 8 * c + 2 * u;
-                            const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[u]);
-                            const float z0 = __low2float(z2), z1 = __high2float(z2);
-                            const float y0 = (w_s[dv] * bf16r(o[j] * rstd)) * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
-                            const float y1 =
-                                (w_s[dv + 1] * bf16r(o[j + 1] * rstd)) * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
-                            outw[4 * m + u] = pack_bf16(y0, y1);
+                            const int j = 8 * m + 2 * u;
+                            outw[4 * m + u] = pack_bf16(bf16r(o[j] * rstd) * gg[2 * u], bf16r(o[j + 1] * rstd) * gg[2 * u + 1]);
                         }
                     }
                 }
@@ -747,12 +772,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     for (int m = 0; m < 4; ++m)
                         dst[eq + 4 * m] = make_uint4(outw[4 * m], outw[4 * m + 1], outw[4 * m + 2], outw[4 * m + 3]);
                 }
-                csync();  // o and z tile read
-                if (tid == 0 && !*abort_flag && p.gated && n + 2 < NC) {  // this parity's z tile takes chunk n + 2
-                    ptx::fence_proxy_async_smem();
-                    load_zt(n + 2);
-                    prefetch_tile(&p.tm_z, h, n + 3);
-                }
+                csync();  // o tile and gate tile read
             }
             // Abort path: wait (bounded) for the z loads and the chain's o copies armed here
             if (*abort_flag && tid == 0) {
