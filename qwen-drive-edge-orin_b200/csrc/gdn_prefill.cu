@@ -14,9 +14,11 @@
 //   C4  dS^T = (v_new e^{c_L-c})^T K                                 tcgen05, M=128, N=128
 //   C3  o^T  = scale e^c (S^T q^T) + v_new^T M^T  (two accumulators)  tcgen05, M=128
 //   --  S <- e^{c_L} S + dS (fp32 registers) while C3 runs; o -> gated RMSNorm -> y
-// Thread 0 issues every MMA (an issue occupies the thread for about the
-// instruction's execution time); dS, S^T q^T and v_new^T M^T commit to separate
-// barriers so that the state update and the new state operand overlap C3.
+//   --  gate = w * silu(z) by every thread while C12 runs; read by the norm epilogue
+// Thread 0 issues the MMAs but v_new^T M^T, which thread 32 issues once dS is in the
+// tensor pipe (an issue occupies the thread for about the instruction's execution
+// time); dS, S^T q^T and v_new^T M^T commit to separate barriers so that the state
+// update and the new state operand overlap C3.
 // Transposed forms put the 128-wide feature dimension on the MMA M axis so
 // every accumulator row is one TMEM lane, which makes the state update
 // thread-local; the norm epilogue re-reads o through a swizzled shared tile
