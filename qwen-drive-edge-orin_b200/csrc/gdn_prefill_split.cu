@@ -36,6 +36,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "gdn_common.cuh"
 #include "gdn_prefill.h"
 #include "sm100_ptx.cuh"
@@ -1017,9 +1019,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 // The compiled count is checked once per device and the kernel is not launched unless
 // it matches.
 static cudaError_t split_prepare(int dev) {
-    static int state[64] = {};  // 0 unchecked, 1 ready, 2 unusable
+    // 0 unchecked, 1 ready, 2 unusable; threads that race here do the same idempotent checks
+    static std::atomic<int> state[64] = {};
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (state[dev] == 0) {
+    if (state[dev].load(std::memory_order_acquire) == 0) {
         int ok = 1;
         for (auto fn : {split::gdn_prefill_split_kernel<false>, split::gdn_prefill_split_kernel<true>}) {
             cudaFuncAttributes fa;
@@ -1032,9 +1035,9 @@ static cudaError_t split_prepare(int dev) {
             e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::SMEM_ALLOC);
             if (e != cudaSuccess) return e;
         }
-        state[dev] = ok ? 1 : 2;
+        state[dev].store(ok ? 1 : 2, std::memory_order_release);
     }
-    return state[dev] == 1 ? cudaSuccess : cudaErrorNotSupported;
+    return state[dev].load(std::memory_order_acquire) == 1 ? cudaSuccess : cudaErrorNotSupported;
 }
 
 bool split_available() {
@@ -1077,10 +1080,10 @@ int split_cluster_ctas() { return split::CLUSTER; }
 // occupancy API (clusters must fit inside a GPC, so this can be below SMs / cluster size;
 // 32 on B200 against 148 / 4 = 37); 0 if the kernel cannot run. Cached per device.
 int split_clusters_per_wave() {
-    static int cache[64] = {};
+    static std::atomic<int> cache[64] = {};  // 0 unknown, -1 no answer, else clusters per wave
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-    if (cache[dev] == 0) {
+    if (cache[dev].load(std::memory_order_acquire) == 0) {
         if (split_prepare(dev) != cudaSuccess) return 0;
         cudaLaunchConfig_t cfg;
         memset(&cfg, 0, sizeof(cfg));
@@ -1099,9 +1102,10 @@ int split_clusters_per_wave() {
             cudaGetLastError();  // clear it: the caller falls back to SMs / cluster size
             n = -1;
         }
-        cache[dev] = n;
+        cache[dev].store(n, std::memory_order_release);
     }
-    return cache[dev] > 0 ? cache[dev] : 0;
+    const int n = cache[dev].load(std::memory_order_acquire);
+    return n > 0 ? n : 0;
 }
 
 }  // namespace gdn
