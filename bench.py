@@ -413,7 +413,25 @@ def cpu_sample_inputs(cfg):
 
 
 # ----------------------------------------------------------------- main
+# The one JSON line goes to the process's original stdout; everything else that writes to file
+# descriptor 1 (NCCL's version banner, library notices from C code) is sent to stderr, so that
+# rank 0's stdout holds the JSON line alone.
+_JSON_OUT = None
+
+
+def emit(line):
+    print(json.dumps(line), file=_JSON_OUT or sys.stdout, flush=True)
+
+
+def _stdout_to_stderr():
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
 def main():
+    _stdout_to_stderr()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -445,10 +463,6 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        # keep rank 0's stdout to the one JSON line: NCCL prints its version banner at WARN and
-        # above, to stdout unless told otherwise
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
     if args.shard_of > 1 and world == 1:  # one rank's share of an N-GPU job, alone on this GPU
@@ -572,7 +586,7 @@ def main():
             "clocks": clk.summary(), "gpu_launches": args.steps * wl.launches_per_step, "status_word": status,
             "graph": graph, "verification": verification, "config4": cfg4, "impl": "ours",
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -675,7 +689,7 @@ def run_reference(args, cfg, world, rank, warmup):
             "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads, "kind": "reference",
                              "sample": desc},
             "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 if __name__ == "__main__":
