@@ -120,10 +120,16 @@ cudaError_t deltanet_chunk_prefill_varlen(
  * and from the identity with v = 0 (final states A_j and Phi_j, one grid), the
  * scan S_0 = initial_state, S_{j+1} = Phi_j S_j + A_j of the segments' entry
  * states, and every segment from its entry state (the output, and the final
- * state of the last segment). The workspace must hold
+ * state of the last segment). The passes run one CTA per (segment, head) or a
+ * 4-CTA cluster per (segment, head), whichever the wave model finds cheaper
+ * (GDN_B200_KERNEL=fused|split restricts the choice). The workspace must hold
  * deltanet_segmented_workspace_size(...) bytes for the same arguments and device
- * (256 when one pass is chosen). */
+ * (256 when one pass is chosen). deltanet_segmented_plan reports the choice:
+ * segments per sequence, chunks per segment, kernel (0: one pass, the plain call;
+ * 1: one CTA per (segment, head); 2: cluster split). */
 size_t deltanet_segmented_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size, int segments);
+cudaError_t deltanet_segmented_plan(int B, int T, int HV, int segments, int* nseg, int* chunks_per_segment,
+                                    int* kernel);
 cudaError_t deltanet_chunk_prefill_segmented(
     const void* q, const void* k, const void* v,
     const float* g, const float* beta,

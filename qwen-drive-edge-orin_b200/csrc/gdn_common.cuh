@@ -51,14 +51,15 @@ struct Params {
     // that the bounded wait for it runs out and the abort path runs. Set only by
     // deltanet_test_withheld_load.
     int withhold_v_chunk;
-    // Segments of long sequences (deltanet_chunk_prefill_segmented; cluster-split kernel only).
+    // Segments of long sequences (deltanet_chunk_prefill_segmented; the kernels' segmented instantiations).
     // seg_chunks > 0: block z indexes (sequence b, segment j) = (z / seg_per_seq, z % seg_per_seq)
     // and covers tokens [j * seg_chunks * 64, min((j + 1) * seg_chunks * 64, T)) of batch row b.
     int seg_chunks, seg_per_seq;
     // State pass of a segmented call (grid y = 2 HV): blocks with blockIdx.y >= HV run v-head
-    // blockIdx.y - HV from the identity state with v read through tm_v0 (a map over a zero tile,
-    // every other box out of bounds, so every load is zero); the others run from a zero state
-    // (s0 null). Each block writes its final state at index (z, blockIdx.y) of sf.
+    // blockIdx.y - HV from the identity state with v = 0 (the cluster-split kernel reads it through
+    // tm_v0, a map over a zero tile, every other box out of bounds, so every load is zero; the
+    // one-CTA kernel loads no v); the others run from a zero state (s0 null). Each block writes its
+    // final state at index (z, blockIdx.y) of sf, the identity runs' transposed (the scan's layout).
     CUtensorMap tm_v0;
     // Output pass of a segmented call: only the last segment of each sequence writes its final
     // state, at sf[b] (the other segments' final states are the next segments' entry states).

@@ -122,14 +122,28 @@ constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192
 // The pre-stage (TRT adapter) mode and the debug dumps are template parameters: the
 // instantiation that serves the plain and gated paths carries neither's code in its loop
 // (the kernel is sensitive to instruction fetch; its loop body is larger than an SM's
-// instruction cache).
-template <bool kPrestage, bool kDebug>
+// instruction cache). So are the passes of a segmented call (kSeg, below).
+//
+// kSeg = SEG_OUTPUT: output pass of a segmented call. Block z indexes (sequence b, segment j) =
+//   (z / seg_per_seq, z % seg_per_seq), covering tokens [j seg_chunks 64, min((j+1) seg_chunks 64, T))
+//   of batch row b, from the entry state s0[z]; only the last segment of each sequence writes its
+//   final state, at sf[b].
+// kSeg = SEG_STATE: state pass. The same segments, grid y = 2 HV: blocks y < HV run v-head y from
+//   a zero state (s0 null), blocks y >= HV v-head y - HV from the identity with v = 0 (no v load,
+//   no v^T T'^T term); each writes its final state at sf[z][y] (an identity run's transposed, the
+//   layout the entry-state scan reads). Nothing else is formed: no q load, no M, no output
+//   products, no norm, no stores but the final state.
+constexpr int SEG_NONE = 0, SEG_OUTPUT = 1, SEG_STATE = 2;
+template <bool kPrestage, bool kDebug, int kSeg = SEG_NONE>
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
+    constexpr bool kState = (kSeg == SEG_STATE);
+    // identity run of a state pass (v = 0, identity entry state)
+    const bool phi_unit = kState && (int)blockIdx.y >= p.HV;
     // the tensor maps are kernel parameters, not data of the previous launch: fetch them while it ends
     if (threadIdx.x == 0) {
-        ptx::prefetch_tensormap(&p.tm_q);
+        if (!kState) ptx::prefetch_tensormap(&p.tm_q);
         ptx::prefetch_tensormap(&p.tm_k);
-        ptx::prefetch_tensormap(&p.tm_v);
+        if (!phi_unit) ptx::prefetch_tensormap(&p.tm_v);
         if (p.gated) ptx::prefetch_tensormap(&p.tm_z);
     }
     // inputs may come from the previous launch in the stream: nothing global is touched before this
@@ -142,12 +156,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;  // TMEM lane of this thread for M=128 accumulators
-    const int h = blockIdx.y;
+    const int h = phi_unit ? (int)blockIdx.y - p.HV : (int)blockIdx.y;
     const int seq = blockIdx.z;
     const int hq = h / (p.HV / p.HQK);
 
     int t_begin, len, bcoord;
-    if (p.cu_seqlens != nullptr) {
+    if (kSeg != SEG_NONE) {  // segment seq % seg_per_seq of batch row seq / seg_per_seq
+        bcoord = seq / p.seg_per_seq;
+        t_begin = (seq - bcoord * p.seg_per_seq) * p.seg_chunks * CS;
+        len = min(p.seg_chunks * CS, p.T - t_begin);
+    } else if (p.cu_seqlens != nullptr) {
         t_begin = p.cu_seqlens[seq];
         len = p.cu_seqlens[seq + 1] - t_begin;
         bcoord = 0;
@@ -205,7 +223,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         for (int j = 0; j < 64; ++j) {
             const int dk = 64 * half + j;
             // plain load: the adapter passes the same buffer as s0 and sf (read here, written at exit)
-            S[j] = (p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f;
+            S[j] = phi_unit ? (dk == row ? 1.f : 0.f) : ((p.s0 != nullptr) ? p.s0[sbase + (size_t)dk * HD + row] : 0.f);
         }
         store_state_operand();
     }
@@ -272,9 +290,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     auto commit = [&]() { commit_to(BAR_MMA); };
 
     if (tid == 0 && NC > 0) {
-        load_q(0);
+        if (!kState) load_q(0);
         load_k(0);
-        if (p.withhold_v_chunk != 0) load_v(0);
+        if (p.withhold_v_chunk != 0 && !phi_unit) load_v(0);
     }
     if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z feeds the gate product (while C12 runs)
     // Gate inputs of the next chunk are prefetched into warp 1's registers (lane l: tokens 2l,
@@ -365,8 +383,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ed_s[2 * lane + 1] = ex2f((cL - c1) * LOG2E);
         }
 
-        // ---- P1: [Q;K] K^T ----
-        wait_bar(BAR_Q, ph);
+        // ---- P1: [Q;K] K^T (a state pass loads no q: rows 0-63 of the product are not read) ----
+        if (!kState) wait_bar(BAR_Q, ph);
         wait_bar(BAR_K, ph);
         if (kPrestage) {
             // fp16 q/k rows -> fp32 L2 normalisation (eps 1e-6 inside the rsqrt) -> bf16, in
@@ -416,6 +434,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ptx::tmem_ld32(tl + TM_P + 32 * half, v);
             ptx::tmem_wait_ld();
             if (row < CS) {
+              if (!kState) {
                 const int i = row;
                 const float ci = c_s[i];
                 float m[32];
@@ -429,6 +448,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                     const uint32_t co = sw_chunk(i, 4 * half + ch, 64);
                     put8_split(sb + OFF_M_HI + co, sb + OFF_M_LO + co, m + 8 * ch, true);
                 }
+              }
             } else {  // L row i: beta_i k_i.k_j e^{c_i - c_j}, j < i
                 const int i = row - CS;
                 const float ci = c_s[i], bi = beta_s[i];
@@ -478,7 +498,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 put8_split(sb + OFF_TPP_HI + co, sb + OFF_TPP_LO + co, tpp + 8 * hh, true);
             }
         }
-        wait_bar(BAR_V, ph);
+        if (!phi_unit) wait_bar(BAR_V, ph);
         if (kPrestage) {  // fp16 v -> bf16 in place (gdnChunkPrefillSm87.cu:88-98); each thread its own words
 #pragma unroll
             for (int e = tid; e < 1024; e += NTHREADS) {
@@ -508,12 +528,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             commit();
             // C12's state-free part v^T [T'_hi; T'_lo]^T into the dS columns (dS of the previous
             // chunk has been read): cols 0-63 the hi terms, 64-127 the lo terms (B stacked along N).
-            // The next commit (after C12's state part) covers it.
+            // The next commit (after C12's state part) covers it. (Zero in an identity run.)
+            if (!phi_unit) {
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const uint64_t a = desc(dlo8k, OFF_V + s * 2048);
-                const uint64_t b = desc(dlo16, OFF_TP_HI + s * 32);
-                ptx::mma_bf16(tmem + TM_C12, a, b, ID_U, s > 0);
+                for (int s = 0; s < 4; ++s) {
+                    const uint64_t a = desc(dlo8k, OFF_V + s * 2048);
+                    const uint64_t b = desc(dlo16, OFF_TP_HI + s * 32);
+                    ptx::mma_bf16(tmem + TM_C12, a, b, ID_U, s > 0);
+                }
             }
         }
         wait_mma();
@@ -551,7 +573,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
                     const uint64_t b = desc(dlo16k, OFF_W_HI + s * 2048);
-                    ptx::mma_bf16_ts(tmem + TM_C12, tmem + sa + 8 * s, b, part ? ID_WS_HI : ID_WS, 1u);
+                    // an identity run has no v^T T'^T term: its first product initialises the columns
+                    ptx::mma_bf16_ts(tmem + TM_C12, tmem + sa + 8 * s, b, part ? ID_WS_HI : ID_WS,
+                                     (!phi_unit || (part | s) > 0) ? 1u : 0u);
                 }
             }
             commit();
@@ -586,7 +610,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             }
         }
         wait_mma();
-        if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk && !*abort_flag) load_v(n + 1);  // v tile consumed
+        if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk && !phi_unit && !*abort_flag)
+            load_v(n + 1);  // v tile consumed
         {   // v_new^T (fp32, cols TM_C12) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
             {
@@ -602,7 +627,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) rec[DBG_VN + (32 * half + jj) * HD + row] = v[jj];
             }
-            {   // v_new hi/lo -> cols [0, 64) (the consumed P1 accumulator)
+            if (!kState) {   // v_new hi/lo -> cols [0, 64) (the consumed P1 accumulator), for v_new^T M^T
                 uint32_t vh[16], vl[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) split2x(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
@@ -642,18 +667,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
             }
             commit_to(BAR_DS);
-            ptx::mbar_arrive(bar(BAR_DSI));  // dS is in the tensor pipe ahead of the output products
+            if (!kState) {
+                ptx::mbar_arrive(bar(BAR_DSI));  // dS is in the tensor pipe ahead of the output products
 #pragma unroll
-            for (int part = 0; part < 2; ++part) {
-                const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
+                for (int part = 0; part < 2; ++part) {
+                    const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
 #pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const uint64_t b = desc(dlo16, OFF_QK + (s >> 2) * 16384 + (s & 3) * 32);
-                    ptx::mma_bf16_ts(tmem + TM_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
+                    for (int s = 0; s < 8; ++s) {
+                        const uint64_t b = desc(dlo16, OFF_QK + (s >> 2) * 16384 + (s & 3) * 32);
+                        ptx::mma_bf16_ts(tmem + TM_O, tmem + sa + 8 * s, b, ID_O, (part | s) > 0);
+                    }
                 }
+                commit_to(BAR_O1);
             }
-            commit_to(BAR_O1);
-        } else if (tid == 32) {
+        } else if (tid == 32 && !kState) {
             // v_new^T M^T on a second issuing thread: an MMA issue occupies its thread for about the
             // instruction's execution time, and on thread 0 alone the 36 MMAs held warp 0 back from
             // its state update. (VN_hi, M_hi), (VN_lo, M_hi), (VN_hi, M_lo)
@@ -691,6 +718,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
             }
+        }
+        if (kState) {  // C12 has read the old state operand and dS the k tile
+            if (tid == 0 && n + 1 < NC && !*abort_flag) load_k(n + 1);
+            store_state_operand();
+            ptx::tmem_wait_st();
+            ptx::tc_fence_before();
+            __syncthreads();
+            continue;
         }
         wait_bar(BAR_O1, consumed[BAR_O1] & 1u);  // S^T q^T has read the old state operand and q
         ptx::tc_fence_after();
@@ -786,13 +821,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         __syncthreads();
     }
 
-    // ---- final state ----
+    // ---- final state: at (seq, h); in a state pass at (segment, grid row) of its 2 HV rows; in an
+    //      output pass only the last segment's, at (batch row, h) ----
     if (!*abort_flag) {
-        const size_t sbase = ((size_t)seq * p.HV + h) * HD * HD;
+        float* sfp = p.sf + ((size_t)seq * p.HV + h) * HD * HD;
+        if (kSeg == SEG_STATE) sfp = p.sf + ((size_t)seq * gridDim.y + blockIdx.y) * HD * HD;
+        if (kSeg == SEG_OUTPUT)
+            sfp = (seq % p.seg_per_seq == p.seg_per_seq - 1) ? p.sf + ((size_t)(seq / p.seg_per_seq) * p.HV + h) * HD * HD
+                                                            : nullptr;
+        if (phi_unit) {  // the map Phi is stored transposed, PhiT[k][i] = Phi[i][k] (k = row): the scan's layout
+            float4* dst = reinterpret_cast<float4*>(sfp + (size_t)row * HD + 64 * half);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-            const int dk = 64 * half + j;
-            p.sf[sbase + (size_t)dk * HD + row] = S[j];
+            for (int j = 0; j < 16; ++j) dst[j] = make_float4(S[4 * j], S[4 * j + 1], S[4 * j + 2], S[4 * j + 3]);
+        } else if (sfp != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                const int dk = 64 * half + j;
+                sfp[(size_t)dk * HD + row] = S[j];
+            }
         }
     }
     // Abort path: wait (bounded) for this CTA's own TMA copies and MMAs still
@@ -861,7 +907,8 @@ static cudaError_t ensure_smem_attr() {
     const uint64_t bit = (dev < 64) ? (1ull << dev) : 0;
     if (bit && (done_mask.load(std::memory_order_acquire) & bit)) return cudaSuccess;
     for (auto fn : {gdn_prefill_kernel<false, false>, gdn_prefill_kernel<true, false>, gdn_prefill_kernel<false, true>,
-                    gdn_prefill_kernel<true, true>}) {
+                    gdn_prefill_kernel<true, true>, gdn_prefill_kernel<false, false, SEG_OUTPUT>,
+                    gdn_prefill_kernel<false, false, SEG_STATE>}) {
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_ALLOC);
         if (e != cudaSuccess) break;
     }
@@ -924,14 +971,15 @@ struct Launch {
     // 2 cluster split) and the chunk whose v-tile load is withheld (-1 none)
     int force_kernel;
     int withhold_v_chunk;
-    // segmented passes (deltanet_chunk_prefill_segmented; cluster-split kernel): chunks per
-    // segment and segments per sequence (nseq = B * seg_per_seq); the state pass (2 HV heads
-    // in the grid, zero tile v0 for the identity runs, no output) or the output pass (only the
-    // last segment's final state, at sf[b])
+    // segmented passes (deltanet_chunk_prefill_segmented): chunks per segment and segments per
+    // sequence (nseq = B * seg_per_seq); the state pass (2 HV heads in the grid, no output; the
+    // cluster-split kernel reads the identity runs' v through the zero tile v0) or the output pass
+    // (only the last segment's final state, at sf[b]); seg_kernel 1: one CTA per unit, 2: cluster split
     int seg_chunks, seg_per_seq;
     int state_pass;
     const void* v0;
     int sf_last_only;
+    int seg_kernel;
 };
 
 // A Launch with every field cleared and no test hook armed.
@@ -947,7 +995,7 @@ static cudaError_t launch(const Launch& L) {
     if (L.HQK <= 0 || L.HV <= 0 || L.HV % L.HQK != 0) return cudaErrorInvalidValue;
     if (L.T < 0 || L.nseq < 0 || L.HV > 65535 || L.nseq > 65535) return cudaErrorInvalidValue;
     if (!L.q || !L.k || !L.v || (!L.out && !L.state_pass) || !L.sf || !L.ws) return cudaErrorInvalidValue;
-    if (L.state_pass && (!L.v0 || L.seg_chunks <= 0 || L.s0)) return cudaErrorInvalidValue;
+    if (L.state_pass && ((L.seg_kernel == 2 && !L.v0) || L.seg_chunks <= 0 || L.s0)) return cudaErrorInvalidValue;
     if (L.prestage ? (!L.ga || !L.gb || !L.A_log || !L.dt_bias) : (!L.g || !L.beta)) return cudaErrorInvalidValue;
     if (L.ws_bytes < WS_HEADER) return cudaErrorInvalidValue;
     const bool gated = (L.z != nullptr) || (L.w != nullptr);
@@ -995,25 +1043,25 @@ static cudaError_t launch(const Launch& L) {
     p.seg_chunks = L.seg_chunks;
     p.seg_per_seq = L.seg_per_seq;
     p.sf_last_only = L.sf_last_only;
-    if (L.seg_chunks > 0) {  // segmented passes: cluster-split kernel only (the caller checked it can run)
-        if (L.dbg || L.prestage || L.cu || L.nseq != L.B * L.seg_per_seq) return cudaErrorInvalidValue;
-        if (L.state_pass) {
-            if (!make_map(&p.tm_v0, L.v0, 1, CS, 1)) return cudaErrorInvalidValue;  // one zero tile
-        } else {
-            p.tm_v0 = p.tm_v;
-        }
-        return launch_split(p, L.nseq, L.state_pass ? 2 * L.HV : L.HV, L.stream);
-    }
     p.tm_v0 = p.tm_v;
+    if (L.seg_chunks > 0) {  // segmented passes (the caller checked that the chosen kernel can run)
+        if (L.dbg || L.prestage || L.cu || L.nseq != L.B * L.seg_per_seq) return cudaErrorInvalidValue;
+        if (L.state_pass && gated) return cudaErrorInvalidValue;
+        if (L.seg_kernel == 2) {
+            if (L.state_pass && !make_map(&p.tm_v0, L.v0, 1, CS, 1)) return cudaErrorInvalidValue;  // one zero tile
+            return launch_split(p, L.nseq, L.state_pass ? 2 * L.HV : L.HV, L.stream);
+        }
+        if (L.seg_kernel != 1) return cudaErrorInvalidValue;
+    }
 
-    const bool split = !L.dbg && !L.prestage && use_split(L.nseq, L.HV, L.force_kernel);
+    const bool split = L.seg_chunks == 0 && !L.dbg && !L.prestage && use_split(L.nseq, L.HV, L.force_kernel);
     if (L.force_kernel == 2 && !split) return cudaErrorNotSupported;
     if (split) return launch_split(p, L.nseq, L.HV, L.stream);
     cudaError_t e = ensure_smem_attr();
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(1, L.HV, L.nseq);
+    cfg.gridDim = dim3(1, L.seg_chunks > 0 && L.state_pass ? 2 * L.HV : L.HV, L.nseq);
     cfg.blockDim = dim3(NTHREADS, 1, 1);
     cfg.dynamicSmemBytes = SMEM_ALLOC;
     cfg.stream = L.stream;
@@ -1025,6 +1073,8 @@ static cudaError_t launch(const Launch& L) {
     cfg.numAttrs = 1;
     void (*kernel)(Params) = L.prestage ? (L.dbg ? gdn_prefill_kernel<true, true> : gdn_prefill_kernel<true, false>)
                                         : (L.dbg ? gdn_prefill_kernel<false, true> : gdn_prefill_kernel<false, false>);
+    if (L.seg_chunks > 0)
+        kernel = L.state_pass ? gdn_prefill_kernel<false, false, SEG_STATE> : gdn_prefill_kernel<false, false, SEG_OUTPUT>;
     e = cudaLaunchKernelEx(&cfg, kernel, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
@@ -1063,61 +1113,90 @@ static cudaError_t noalloc_scratch(void** out) {
 // Long sequences in segments (deltanet_chunk_prefill_segmented).
 constexpr size_t SEG_ZERO_BYTES = (size_t)CS * HD * 2;  // one zero bf16 tile [64 tok][128]: the identity runs' v
 
-// Segments per sequence for B sequences of NC chunks and HV v-heads, `wave` clusters of the
-// cluster-split kernel at once, from a wave model: a wave of clusters costs its chunks' periods
-// plus about WAVE_OVERHEAD periods of start-up and drain (the first chunk's preparation and
-// shipment before the chain can start, the last chunk's output after it), so the segmented call
-// costs (waves of 2 U s units + waves of U s units) * (ceil(NC / s) + overhead), U = B HV
-// (state pass, then output pass; the scan is small), against waves(U) * (NC + overhead) for
-// one pass. Returns the cheapest s (1: one pass), the smaller on ties.
-constexpr int WAVE_OVERHEAD = 5;
-static int auto_segments(int B, int HV, int NC, int wave) {
+// Plan of a segmented call: segments per sequence, chunks per segment and the kernel that runs
+// the passes (1: one CTA per (segment, head), 2: cluster split), from a wave model of B200
+// measurements. A wave of units costs its chunk count plus a start-up and drain overhead, times
+// the kernel's chunk period; the call costs the state pass (2 U s units: the zero-state and the
+// identity runs), the scan (one step per segment) and the output pass (U s units), U = B HV.
+//   cluster split: 4 SMs per unit, clusters per wave from the occupancy API (32 on B200: clusters
+//     must fit inside a GPC), ~3.0 us per chunk in either pass, ~5 periods of overhead;
+//   one CTA per unit: one unit per SM, ~10.2 us per chunk in the output pass, ~6 us in the state
+//     pass (no output products, norm or q loads), ~1 period of overhead.
+// One pass (s = 1) costs what the plain call launches. The cheapest plan wins, fewer segments on
+// ties. GDN_B200_KERNEL=fused|split restricts the passes to one kernel.
+struct SegPlan {
+    int nseg, per, kernel;
+};
+constexpr double SPLIT_CHUNK_US = 3.0, FUSED_CHUNK_US = 10.2, STATE_CHUNK_US = 6.0, SCAN_STEP_US = 1.0;
+constexpr int WAVE_OVERHEAD = 5, FUSED_OVERHEAD = 1;
+static SegPlan plan_segments(int B, int HV, int NC, int segments, int sms, int cluster_wave, bool split_ok,
+                             bool fused_ok) {
     const long long U = (long long)B * HV;
-    if (wave <= 0 || NC <= 1) return 1;
-    auto waves = [&](long long units) { return (units + wave - 1) / wave; };
-    long long best_cost = waves(U) * (NC + WAVE_OVERHEAD);
-    int best = 1;
+    auto waves = [](long long units, int wave) { return (double)((units + wave - 1) / wave); };
+    if (cluster_wave <= 0 || sms <= 0) split_ok = false;
+    if (!split_ok) fused_ok = true;  // the one-CTA kernel always runs
+    auto cost = [&](int eff, int per, int kernel) {  // segmented call, `eff` segments of `per` chunks
+        const double scan = eff * SCAN_STEP_US;
+        const long long su = 2 * U * (eff - 1);  // state-pass units: every segment but the last, twice
+        if (kernel == 2)
+            return (waves(su, cluster_wave) + waves(U * eff, cluster_wave)) * (per + WAVE_OVERHEAD) * SPLIT_CHUNK_US +
+                   scan;
+        return waves(su, sms) * (per + FUSED_OVERHEAD) * STATE_CHUNK_US +
+               waves(U * eff, sms) * (per + FUSED_OVERHEAD) * FUSED_CHUNK_US + scan;
+    };
+    auto cheaper_kernel = [&](int eff, int per) {
+        if (!split_ok) return 1;
+        if (!fused_ok) return 2;
+        return cost(eff, per, 1) <= cost(eff, per, 2) ? 1 : 2;
+    };
+    SegPlan best{1, NC, 0};
+    if (NC <= 1) return best;
+    if (segments > 0) {  // an explicit request: that many segments (at most one per chunk), whatever one pass costs
+        const int s = segments < NC ? segments : NC;
+        const int per = (NC + s - 1) / s, eff = (NC + per - 1) / per;
+        if (eff <= 1) return best;
+        return SegPlan{eff, per, sms > 0 ? cheaper_kernel(eff, per) : (split_ok ? 2 : 1)};
+    }
+    if (sms <= 0) return best;
+    // one pass: the plain call's kernel choice (cluster split while the clusters fit in two waves)
+    double best_cost = (split_ok && U <= 2LL * (sms / 4))
+                           ? waves(U, cluster_wave) * (NC + WAVE_OVERHEAD) * SPLIT_CHUNK_US
+                           : waves(U, sms) * (NC + FUSED_OVERHEAD) * FUSED_CHUNK_US;
     for (int s = 2; s <= NC && s <= 256; ++s) {
-        const long long per = (NC + s - 1) / s;
-        const long long eff = (NC + per - 1) / per;  // segments actually made with `per` chunks each
-        if (eff != s) continue;
-        const long long cost = (waves(2 * U * s) + waves(U * s)) * (per + WAVE_OVERHEAD);
-        if (cost < best_cost) {
-            best_cost = cost;
-            best = s;
+        const int per = (NC + s - 1) / s;
+        if ((NC + per - 1) / per != s) continue;  // `per` chunks each make fewer segments
+        const int k = cheaper_kernel(s, per);
+        const double c = cost(s, per, k);
+        if (c < best_cost) {
+            best_cost = c;
+            best = SegPlan{s, per, k};
         }
     }
     return best;
 }
 
-// (segments per sequence, chunks per segment) actually used for a request of `segments`
-// (0: automatic on the current device).
-static void resolve_segments(int B, int T, int HV, int segments, int* nseg, int* per) {
+// The plan for a request of `segments` (0: automatic) on the current device.
+static SegPlan resolve_segments(int B, int T, int HV, int segments) {
     const int NC = (T + CS - 1) / CS;
-    int s = segments;
-    if (s <= 0) {
-        int wave = split_clusters_per_wave();
-        if (wave <= 0) {  // no occupancy answer: SMs / cluster size
-            int dev = 0, sms = 0;
-            if (cudaGetDevice(&dev) == cudaSuccess &&
-                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
-                wave = sms / split_cluster_ctas();
-        }
-        s = auto_segments(B, HV, NC, wave);
-    }
-    if (NC <= 1 || s <= 1) {
-        *nseg = 1;
-        *per = NC;
-        return;
-    }
-    s = s < NC ? s : NC;
-    *per = (NC + s - 1) / s;
-    *nseg = (NC + *per - 1) / *per;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        sms = 0;
+    const char* env = getenv("GDN_B200_KERNEL");
+    bool split_ok = split_available(), fused_ok = true;
+    if (env && strcmp(env, "fused") == 0) split_ok = false;
+    if (env && strcmp(env, "split") == 0) fused_ok = false;
+    int wave = split_ok ? split_clusters_per_wave() : 0;
+    if (split_ok && wave <= 0) wave = sms / split_cluster_ctas();  // no occupancy answer: SMs / cluster size
+    SegPlan pl = plan_segments(B, HV, NC, segments, sms, wave, split_ok, fused_ok);
+    if (pl.kernel == 0 || pl.nseg <= 1) pl = SegPlan{1, NC, 0};
+    return pl;
 }
 
+// status header, the zero tile, the state pass's maps A_j and PhiT_j of every segment but the
+// last ([B (nseg - 1)][2 HV][128][128] fp32) and the entry states ([B nseg][HV][128][128] fp32)
 static size_t segmented_bytes(int B, int HV, int nseg) {
     if (nseg <= 1) return WS_HEADER;
-    return WS_HEADER + SEG_ZERO_BYTES + (size_t)B * nseg * 3 * HV * HD * HD * sizeof(float);
+    return WS_HEADER + SEG_ZERO_BYTES + (size_t)B * (3 * nseg - 2) * HV * HD * HD * sizeof(float);
 }
 
 static size_t debug_bytes(int B, int T, int HV) {
@@ -1140,9 +1219,22 @@ size_t deltanet_prefill_workspace_size(int B, int T, int HV, int DK, int DV, int
 size_t deltanet_segmented_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size, int segments) {
     (void)DK; (void)DV; (void)chunk_size;
     if (B <= 0 || T <= 0 || HV <= 0) return gdn::WS_HEADER;
-    int nseg = 1, per = 1;
-    gdn::resolve_segments(B, T, HV, segments, &nseg, &per);
-    return gdn::segmented_bytes(B, HV, nseg);
+    return gdn::segmented_bytes(B, HV, gdn::resolve_segments(B, T, HV, segments).nseg);
+}
+
+// The plan deltanet_chunk_prefill_segmented makes for these sizes on the current device: segments
+// per sequence, chunks per segment and the kernel of its passes (0: one pass, the plain call;
+// 1: one CTA per (segment, head); 2: cluster split).
+cudaError_t deltanet_segmented_plan(int B, int T, int HV, int segments, int* nseg, int* chunks_per_segment,
+                                    int* kernel) {
+    if (!nseg || !chunks_per_segment || !kernel || segments < 0 || B < 0 || T < 0 || HV <= 0)
+        return cudaErrorInvalidValue;
+    gdn::SegPlan pl{1, (T + gdn::CS - 1) / gdn::CS, 0};
+    if (B > 0 && T > 0) pl = gdn::resolve_segments(B, T, HV, segments);
+    *nseg = pl.nseg;
+    *chunks_per_segment = pl.per;
+    *kernel = pl.kernel;
+    return cudaSuccess;
 }
 
 size_t deltanet_prefill_debug_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size) {
@@ -1274,9 +1366,9 @@ cudaError_t deltanet_chunk_prefill_segmented(const void* q, const void* k, const
                                              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     if ((z == nullptr) != (norm_w == nullptr) || segments < 0) return cudaErrorInvalidValue;
     if (DK != gdn::HD || DV != gdn::HD || chunk_size != gdn::CS || B < 0 || T < 0 || HV <= 0) return cudaErrorInvalidValue;
-    int nseg = 1, per = 1;
-    if (B > 0 && T > 0) gdn::resolve_segments(B, T, HV, segments, &nseg, &per);
-    if (nseg > 1 && !gdn::split_available()) nseg = 1;  // the segmented passes need the cluster-split kernel
+    gdn::SegPlan plan{1, 1, 0};
+    if (B > 0 && T > 0) plan = gdn::resolve_segments(B, T, HV, segments);
+    const int nseg = plan.nseg, per = plan.per;
     if (nseg <= 1)  // one pass is the plain call
         return z ? deltanet_chunk_prefill_gated(q, k, v, g, beta, z, norm_w, eps, out, initial_state, final_state, B, T,
                                                 HV, HQK, DK, DV, chunk_size, workspace, workspace_bytes, stream)
@@ -1285,23 +1377,26 @@ cudaError_t deltanet_chunk_prefill_segmented(const void* q, const void* k, const
     if (!workspace || workspace_bytes < gdn::segmented_bytes(B, HV, nseg)) return cudaErrorInvalidValue;
     char* ws = static_cast<char*>(workspace);
     void* zero = ws + gdn::WS_HEADER;
-    float* stt = reinterpret_cast<float*>(ws + gdn::WS_HEADER + gdn::SEG_ZERO_BYTES);  // [B nseg][2 HV][D][D]
-    float* entry = stt + (size_t)B * nseg * 2 * HV * gdn::HD * gdn::HD;                 // [B nseg][HV][D][D]
+    float* stt = reinterpret_cast<float*>(ws + gdn::WS_HEADER + gdn::SEG_ZERO_BYTES);  // [B (nseg-1)][2 HV][D][D]
+    float* entry = stt + (size_t)B * (nseg - 1) * 2 * HV * gdn::HD * gdn::HD;           // [B nseg][HV][D][D]
     cudaError_t e = cudaMemsetAsync(zero, 0, gdn::SEG_ZERO_BYTES, stream);
     if (e != cudaSuccess) return e;
     gdn::Launch L = gdn::blank_launch();
     L.q = q; L.k = k; L.v = v; L.g = g; L.beta = beta; L.eps = eps;
-    L.nseq = B * nseg; L.B = B; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
+    L.B = B; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
     L.max_nc = per;
     L.ws = workspace; L.ws_bytes = workspace_bytes; L.stream = stream;
-    L.seg_chunks = per; L.seg_per_seq = nseg;
-    // state pass: A_j (zero entry, v) at heads [0, HV), Phi_j (identity entry, zero v) at [HV, 2 HV)
+    L.seg_chunks = per; L.seg_kernel = plan.kernel;
+    // state pass over the first nseg - 1 segments of each sequence (the last one's maps are not
+    // needed): A_j (zero entry, v) at heads [0, HV), PhiT_j (identity entry, zero v) at [HV, 2 HV)
+    L.nseq = B * (nseg - 1); L.seg_per_seq = nseg - 1;
     L.state_pass = 1; L.v0 = zero; L.sf = stt; L.out = nullptr;
     e = gdn::launch(L);
     if (e != cudaSuccess) return e;
     e = gdn::launch_segment_scan(stt, initial_state, entry, B, HV, nseg, stream);
     if (e != cudaSuccess) return e;
-    // output pass from the entry states; the last segment's final state is the sequence's
+    // output pass over every segment from its entry state; the last segment's final state is the sequence's
+    L.nseq = B * nseg; L.seg_per_seq = nseg;
     L.state_pass = 0; L.v0 = nullptr; L.z = z; L.w = norm_w; L.out = out;
     L.s0 = entry; L.sf = final_state; L.sf_last_only = 1;
     return gdn::launch(L);

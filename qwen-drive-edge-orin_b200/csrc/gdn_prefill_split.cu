@@ -495,7 +495,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 if (kSeg && p.sf_last_only)
                     sfp = (seq % p.seg_per_seq == p.seg_per_seq - 1)
                               ? p.sf + ((size_t)(seq / p.seg_per_seq) * p.HV + h) * HD * HD : nullptr;
-                if (sfp != nullptr) {
+                if (phi_unit) {  // the map Phi is stored transposed, PhiT[k][i] = Phi[i][k] (k = row)
+                    float4* dst = reinterpret_cast<float4*>(sfp + (size_t)row * HD + 64 * half);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) dst[j] = make_float4(S[4 * j], S[4 * j + 1], S[4 * j + 2], S[4 * j + 3]);
+                } else if (sfp != nullptr) {
 #pragma unroll
                     for (int j = 0; j < 64; ++j) sfp[(size_t)(64 * half + j) * HD + row] = S[j];
                 }

@@ -22,6 +22,7 @@ from .binding import (  # noqa: F401
     chunk_prefill_gated,
     chunk_prefill_varlen,
     chunk_prefill_segmented,
+    segmented_plan,
     segment_bounds,
     segment_entry_states,
     run_chunk_prefill,

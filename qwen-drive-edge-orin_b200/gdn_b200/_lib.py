@@ -30,6 +30,7 @@ SIGNATURES = {
                                                                c_void_p, c_int] + [c_int] * 6
                                       + [c_void_p, c_size_t, c_void_p]),
     "deltanet_segmented_workspace_size": (c_size_t, [c_int] * 7),
+    "deltanet_segmented_plan": (c_int, [c_int] * 4 + [ctypes.POINTER(c_int)] * 3),
     "deltanet_chunk_prefill_segmented": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p, c_void_p]
                                          + [c_int] * 8 + [c_void_p, c_size_t, c_void_p]),
     "deltanet_chunk_prefill_gated_noalloc": (c_int, [c_void_p] * 7 + [c_float, c_void_p, c_void_p, c_void_p]

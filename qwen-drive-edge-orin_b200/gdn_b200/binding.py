@@ -273,6 +273,19 @@ def segment_entry_states(Phi, A, s0=None):
     return torch.stack(states, dim=1).view(B, HV, nseg, d, d).transpose(1, 2).float().contiguous()
 
 
+def segmented_plan(B: int, T: int, HV: int, segments: int = 0):
+    """The plan ``deltanet_chunk_prefill_segmented`` makes for these sizes on the current device:
+    (segments per sequence, chunks per segment, kernel), kernel 0 = one pass (the plain call),
+    1 = one CTA per (segment, head), 2 = a 4-CTA cluster per (segment, head)."""
+    if B < 0 or T < 0 or HV <= 0 or segments < 0:
+        raise ValueError("B, T >= 0, HV > 0 and segments >= 0 required")
+    lib = load_library()
+    nseg, per, kernel = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _check(lib.deltanet_segmented_plan(B, T, HV, segments, ctypes.byref(nseg), ctypes.byref(per), ctypes.byref(kernel)),
+           "deltanet_segmented_plan")
+    return nseg.value, per.value, kernel.value
+
+
 def chunk_prefill_segmented(q, k, v, g, beta, s0=None, z=None, w=None, eps: float = 1e-6,
                             segments: int | None = None):
     """Prefill of long sequences cut into segments that run in parallel: [o or y, final_state].

@@ -39,11 +39,20 @@ def _run(fn, inp, gated, **kw):
     return [t.float().cpu().numpy() for t in out]
 
 
+@pytest.mark.parametrize("kernel", ["fused", "split"])
 @pytest.mark.parametrize("B,T,HQK,HV,segments,gated", [(1, 4133, 2, 4, 5, False), (1, 4133, 2, 4, 5, True),
-                                                        (2, 2000, 2, 4, 3, True), (1, 65, 2, 4, 8, False)])
-def test_segmented_matches_plain(B, T, HQK, HV, segments, gated):
+                                                        (2, 2000, 2, 4, 3, True), (1, 65, 2, 4, 8, False),
+                                                        (1, 2000, 1, 2, 7, True)])
+def test_segmented_matches_plain(B, T, HQK, HV, segments, gated, kernel, monkeypatch):
+    """Both kernels of the segmented passes: one CTA per (segment, head) ("fused") and a 4-CTA
+    cluster per (segment, head) ("split"), chosen through GDN_B200_KERNEL."""
     inp = make_inputs(B, T, HQK, HV, seed=11)
     o_ref, sf_ref = _run("plain", inp, gated)
+    monkeypatch.setenv("GDN_B200_KERNEL", kernel)
+    nseg, per, kern = gdn_b200.segmented_plan(B, T, HV, segments)
+    nc = (T + 63) // 64
+    assert nseg == (nc + per - 1) // per and per == (nc + min(segments, nc) - 1) // min(segments, nc)
+    assert kern == ({"fused": 1, "split": 2}[kernel] if nseg > 1 else 0)
     o, sf = _run("segmented", inp, gated, segments=segments)
     assert o.shape == o_ref.shape and sf.shape == sf_ref.shape
     if gated:
@@ -53,7 +62,8 @@ def test_segmented_matches_plain(B, T, HQK, HV, segments, gated):
     assert tensor_l2_rel(sf, sf_ref) < 1e-4
 
 
-def test_segmented_slow_decay_against_oracle():
+@pytest.mark.parametrize("kernel", ["fused", "split"])
+def test_segmented_slow_decay_against_oracle(kernel, monkeypatch):
     """Slow-decay heads (g = -U(0, 0.002), beta = U(0, 0.3)) with random initial states: each
     segment's state map Phi is far from zero, so the entry states come from the scan rather than
     being forgotten. Five segments of a 4,133-token sequence against the serial oracle and the
@@ -67,6 +77,7 @@ def test_segmented_slow_decay_against_oracle():
                               beta=(rng.random(base.beta.shape) * 0.3).astype(np.float32))
     o_ref, sf_ref = O.chunk_gated_delta_rule(inp.q, inp.k, inp.v, inp.g, inp.beta, 64, inp.s0)
     o_one, sf_one = _run("plain", inp, False)
+    monkeypatch.setenv("GDN_B200_KERNEL", kernel)
     o, sf = _run("segmented", inp, False, segments=5)
     print({"o_abs_oracle": max_abs(o, o_ref), "st_rel_oracle": tensor_l2_rel(sf, sf_ref),
            "o_abs_onepass": max_abs(o, o_one), "st_rel_onepass": tensor_l2_rel(sf, sf_one)})
@@ -105,9 +116,8 @@ def test_config3_shard_library_choice_against_one_pass():
     inp = make_inputs(1, 65536, 2, 4, seed=3, with_s0=False)
     q, k, v, z, w = _dev(inp.q), _dev(inp.k), _dev(inp.v), _dev(inp.z), _dev(inp.w)
     g, b = _dev(inp.g, torch.float32), _dev(inp.beta, torch.float32)
-    lib = gdn_b200.load_library()
-    nbytes = lib.deltanet_segmented_workspace_size(1, 65536, 4, 128, 128, 64, 0)
-    assert nbytes > 256, "the library should cut a 4-head 65,536-token stream into segments"
+    nseg, per, kern = gdn_b200.segmented_plan(1, 65536, 4)
+    assert nseg > 1, "the library should cut a 4-head 65,536-token stream into segments"
     y1, sf1 = gdn_b200.chunk_prefill_gated(q, k, v, g, b, z, w)
     y, sf = gdn_b200.chunk_prefill_segmented(q, k, v, g, b, z=z, w=w)
     torch.cuda.synchronize()
@@ -115,9 +125,8 @@ def test_config3_shard_library_choice_against_one_pass():
     assert max_rel(yh, y1) < Y_MAX_REL and tensor_l2_rel(sfh, sf1) < 1e-4
     t_one = _timed(lambda: gdn_b200.chunk_prefill_gated(q, k, v, g, b, z, w))
     t_seg = _timed(lambda: gdn_b200.chunk_prefill_segmented(q, k, v, g, b, z=z, w=w))
-    nseg = (nbytes - 256 - 16384) // (3 * 4 * 128 * 128 * 4)
     warnings.warn(f"config-3 shard (S=65536, 4 v-heads): one pass {t_one:.3f} ms, segmented "
-                  f"({nseg} segments) {t_seg:.3f} ms")
+                  f"({nseg} segments of {per} chunks, kernel {kern}) {t_seg:.3f} ms")
 
 
 def test_full_gpu_takes_one_pass():
