@@ -128,20 +128,26 @@ constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192
 //   (z / seg_per_seq, z % seg_per_seq), covering tokens [j seg_chunks 64, min((j+1) seg_chunks 64, T))
 //   of batch row b, from the entry state s0[z]; only the last segment of each sequence writes its
 //   final state, at sf[b].
-// kSeg = SEG_STATE: state pass. The same segments, grid y = 2 HV: blocks y < HV run v-head y from
-//   a zero state (s0 null), blocks y >= HV v-head y - HV from the identity with v = 0 (no v load,
-//   no v^T T'^T term); each writes its final state at sf[z][y] (an identity run's transposed, the
-//   layout the entry-state scan reads). Nothing else is formed: no q load, no M, no output
-//   products, no norm, no stores but the final state.
-constexpr int SEG_NONE = 0, SEG_OUTPUT = 1, SEG_STATE = 2;
+// kSeg = SEG_STATE: state pass, the zero-state runs. The same segments (every one but the last),
+//   grid y = HV: v-head y from a zero state (s0 null); writes its final state A at sf[z][y] of the
+//   [z][2 HV] map array, and every chunk's W^T hi/lo tiles to wbuf. Nothing else is formed: no q
+//   load, no M, no output products, no norm.
+// kSeg = SEG_PHI: the identity runs' pass, after it: v-head y from the identity with v = 0. Its
+//   chunk update needs only W (from wbuf), k and the gates, so it forms no chunk preparation (no
+//   P1, L, inverse, T', P3) and loads no q or v; k alternates between the two halves of the
+//   [q; k] panels so that the next chunk's k loads a chunk ahead. Writes its final state, the map
+//   Phi, transposed (the layout the entry-state scan reads) at sf[z][HV + y].
+constexpr int SEG_NONE = 0, SEG_OUTPUT = 1, SEG_STATE = 2, SEG_PHI = 3;
 template <bool kPrestage, bool kDebug, int kSeg = SEG_NONE>
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
     constexpr bool kState = (kSeg == SEG_STATE);
-    // identity run of a state pass (v = 0, identity entry state)
-    const bool phi_unit = kState && (int)blockIdx.y >= p.HV;
+    constexpr bool kPhi = (kSeg == SEG_PHI);
+    constexpr bool kLean = kState || kPhi;  // no q, M, output products or norm
+    // identity run (v = 0, identity entry state)
+    constexpr bool phi_unit = kPhi;
     // the tensor maps are kernel parameters, not data of the previous launch: fetch them while it ends
     if (threadIdx.x == 0) {
-        if (!kState) ptx::prefetch_tensormap(&p.tm_q);
+        if (!kLean) ptx::prefetch_tensormap(&p.tm_q);
         ptx::prefetch_tensormap(&p.tm_k);
         if (!phi_unit) ptx::prefetch_tensormap(&p.tm_v);
         if (p.gated) ptx::prefetch_tensormap(&p.tm_z);
@@ -156,7 +162,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;  // TMEM lane of this thread for M=128 accumulators
-    const int h = phi_unit ? (int)blockIdx.y - p.HV : (int)blockIdx.y;
+    const int h = (int)blockIdx.y;
     const int seq = blockIdx.z;
     const int hq = h / (p.HV / p.HQK);
 
@@ -243,12 +249,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::tma_load_4d(sb + OFF_QK + 0, &p.tm_q, bar(BAR_Q), 0, hq, t, bcoord);
         ptx::tma_load_4d(sb + OFF_QK + 16384, &p.tm_q, bar(BAR_Q), 64, hq, t, bcoord);
     };
+    // Offset of chunk n's k rows inside the [q; k] panels: rows 64-127; an identity-run pass
+    // alternates between rows 64-127 (even chunks) and rows 0-63 (odd chunks).
+    auto koff = [](int n) -> uint32_t { return (kPhi && (n & 1)) ? 0u : 8192u; };
     auto load_k = [&](int n) {
         ++issued[BAR_K];
         ptx::mbar_arrive_expect_tx(bar(BAR_K), 16384);
         const int t = t_begin + n * CS;
-        ptx::tma_load_4d(sb + OFF_QK + 8192, &p.tm_k, bar(BAR_K), 0, hq, t, bcoord);
-        ptx::tma_load_4d(sb + OFF_QK + 16384 + 8192, &p.tm_k, bar(BAR_K), 64, hq, t, bcoord);
+        ptx::tma_load_4d(sb + OFF_QK + koff(n), &p.tm_k, bar(BAR_K), 0, hq, t, bcoord);
+        ptx::tma_load_4d(sb + OFF_QK + 16384 + koff(n), &p.tm_k, bar(BAR_K), 64, hq, t, bcoord);
+    };
+    // W^T hi/lo tiles of chunk n in wbuf, and (identity-run pass) the two shared-memory buffers they
+    // are loaded into (the T'/T'' area is free there); the v barrier counts those loads
+    auto wofs = [&](int n) -> size_t { return ((size_t)(seq * p.HV + h) * p.seg_chunks + n) * 32768; };
+    auto wtile = [](int n) -> uint32_t { return (n & 1) ? OFF_X : OFF_W_HI; };
+    auto load_w = [&](int n) {
+        ++issued[BAR_V];
+        ptx::mbar_arrive_expect_tx(bar(BAR_V), 32768);
+        ptx::bulk_load_g2s(sb + wtile(n), p.wbuf + wofs(n), 32768, bar(BAR_V));
     };
     auto load_v = [&](int n) {
         ++issued[BAR_V];
@@ -290,9 +308,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     auto commit = [&]() { commit_to(BAR_MMA); };
 
     if (tid == 0 && NC > 0) {
-        if (!kState) load_q(0);
+        if (!kLean) load_q(0);
         load_k(0);
         if (p.withhold_v_chunk != 0 && !phi_unit) load_v(0);
+        if (kPhi) load_w(0);
     }
     if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z feeds the gate product (while C12 runs)
     // Gate inputs of the next chunk are prefetched into warp 1's registers (lane l: tokens 2l,
@@ -383,8 +402,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ed_s[2 * lane + 1] = ex2f((cL - c1) * LOG2E);
         }
 
+        if constexpr (kPhi) {
+            // ---- identity run: no chunk preparation; chunk n's k tile, and its W^T tiles as the
+            //      zero-state run of this (segment, head) formed them ----
+            wait_bar(BAR_K, ph);
+            wait_bar(BAR_V, ph);
+            __syncthreads();  // the gates are visible, and every thread is past this chunk's waits
+            if (*abort_flag) break;
+            if (tid == 0 && n + 1 < NC) load_k(n + 1);  // into the other half of the panels
+        } else {
         // ---- P1: [Q;K] K^T (a state pass loads no q: rows 0-63 of the product are not read) ----
-        if (!kState) wait_bar(BAR_Q, ph);
+        if (!kLean) wait_bar(BAR_Q, ph);
         wait_bar(BAR_K, ph);
         if (kPrestage) {
             // fp16 q/k rows -> fp32 L2 normalisation (eps 1e-6 inside the rsqrt) -> bf16, in
@@ -434,7 +462,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             ptx::tmem_ld32(tl + TM_P + 32 * half, v);
             ptx::tmem_wait_ld();
             if (row < CS) {
-              if (!kState) {
+              if (!kLean) {
                 const int i = row;
                 const float ci = c_s[i];
                 float m[32];
@@ -513,6 +541,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 st_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
             }
         }
+        if (kState && tid == 0 && n > 0) ptx::bulk_wait_read_all();  // the W^T tiles' store has read them
         ptx::fence_proxy_async_smem();
         __syncthreads();
 
@@ -561,6 +590,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::fence_proxy_async_smem();
         __syncthreads();
         if (*abort_flag) break;
+        if (kState && tid == 0) ptx::bulk_store_s2g(p.wbuf + wofs(n), sb + OFF_W_HI, 32768);  // for the identity runs
+        }  // chunk preparation
 
         // ---- C12: v_new^T = v^T T'^T - S^T W^T (the v^T T'^T part was issued with P3) ----
         if (tid == 0) {
@@ -572,7 +603,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint32_t sa = part ? TM_SA_LO : TM_SA_HI;
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
-                    const uint64_t b = desc(dlo16k, OFF_W_HI + s * 2048);
+                    const uint64_t b = desc(dlo16k, (kPhi ? wtile(n) : OFF_W_HI) + s * 2048);
                     // an identity run has no v^T T'^T term: its first product initialises the columns
                     ptx::mma_bf16_ts(tmem + TM_C12, tmem + sa + 8 * s, b, part ? ID_WS_HI : ID_WS,
                                      (!phi_unit || (part | s) > 0) ? 1u : 0u);
@@ -612,6 +643,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         wait_mma();
         if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk && !phi_unit && !*abort_flag)
             load_v(n + 1);  // v tile consumed
+        if (kPhi && tid == 0 && n + 1 < NC && !*abort_flag) load_w(n + 1);  // C12 of chunk n - 1 read that buffer
         {   // v_new^T (fp32, cols TM_C12) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
             {
@@ -627,7 +659,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) rec[DBG_VN + (32 * half + jj) * HD + row] = v[jj];
             }
-            if (!kState) {   // v_new hi/lo -> cols [0, 64) (the consumed P1 accumulator), for v_new^T M^T
+            if (!kLean) {   // v_new hi/lo -> cols [0, 64) (the consumed P1 accumulator), for v_new^T M^T
                 uint32_t vh[16], vl[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) split2x(v[2 * j], v[2 * j + 1], vh[j], vl[j]);
@@ -662,12 +694,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 const uint32_t va = part ? TM_VP_LO : TM_VP_HI;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const uint64_t b = desc(dlo16k, OFF_QK + 8192 + s * 2048);
+                    const uint64_t b = desc(dlo16k, OFF_QK + koff(n) + s * 2048);
                     ptx::mma_bf16_ts(tmem + TM_S, tmem + va + 8 * s, b, ID_S, (part | s) > 0);
                 }
             }
             commit_to(BAR_DS);
-            if (!kState) {
+            if (!kLean) {
                 ptx::mbar_arrive(bar(BAR_DSI));  // dS is in the tensor pipe ahead of the output products
 #pragma unroll
                 for (int part = 0; part < 2; ++part) {
@@ -680,7 +712,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
                 commit_to(BAR_O1);
             }
-        } else if (tid == 32 && !kState) {
+        } else if (tid == 32 && !kLean) {
             // v_new^T M^T on a second issuing thread: an MMA issue occupies its thread for about the
             // instruction's execution time, and on thread 0 alone the 36 MMAs held warp 0 back from
             // its state update. (VN_hi, M_hi), (VN_lo, M_hi), (VN_hi, M_lo)
@@ -719,8 +751,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 for (int j = 0; j < 32; ++j) S[32 * c2 + j] = fmaf(gam, S[32 * c2 + j], v[j]);
             }
         }
-        if (kState) {  // C12 has read the old state operand and dS the k tile
-            if (tid == 0 && n + 1 < NC && !*abort_flag) load_k(n + 1);
+        if (kLean) {  // C12 has read the old state operand and dS the k tile
+            if (kState && tid == 0 && n + 1 < NC && !*abort_flag) load_k(n + 1);
             store_state_operand();
             ptx::tmem_wait_st();
             ptx::tc_fence_before();
@@ -825,7 +857,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     //      output pass only the last segment's, at (batch row, h) ----
     if (!*abort_flag) {
         float* sfp = p.sf + ((size_t)seq * p.HV + h) * HD * HD;
-        if (kSeg == SEG_STATE) sfp = p.sf + ((size_t)seq * gridDim.y + blockIdx.y) * HD * HD;
+        if (kLean) sfp = p.sf + ((size_t)seq * 2 * p.HV + (kPhi ? p.HV : 0) + h) * HD * HD;  // the [z][2 HV] maps
         if (kSeg == SEG_OUTPUT)
             sfp = (seq % p.seg_per_seq == p.seg_per_seq - 1) ? p.sf + ((size_t)(seq / p.seg_per_seq) * p.HV + h) * HD * HD
                                                             : nullptr;
@@ -841,6 +873,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             }
         }
     }
+    if (kState && tid == 0) ptx::bulk_wait_all();  // the W^T tiles' stores have completed
     // Abort path: wait (bounded) for this CTA's own TMA copies and MMAs still
     // in flight before its shared memory and TMEM are released.
     if (*abort_flag && (tid == 0 || tid == 32 || tid == 128)) {
@@ -908,7 +941,7 @@ static cudaError_t ensure_smem_attr() {
     if (bit && (done_mask.load(std::memory_order_acquire) & bit)) return cudaSuccess;
     for (auto fn : {gdn_prefill_kernel<false, false>, gdn_prefill_kernel<true, false>, gdn_prefill_kernel<false, true>,
                     gdn_prefill_kernel<true, true>, gdn_prefill_kernel<false, false, SEG_OUTPUT>,
-                    gdn_prefill_kernel<false, false, SEG_STATE>}) {
+                    gdn_prefill_kernel<false, false, SEG_STATE>, gdn_prefill_kernel<false, false, SEG_PHI>}) {
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_ALLOC);
         if (e != cudaSuccess) break;
     }
@@ -980,6 +1013,10 @@ struct Launch {
     const void* v0;
     int sf_last_only;
     int seg_kernel;
+    // one-CTA segmented state passes: the zero-state runs (state_pass) store W^T tiles to wbuf, the
+    // identity runs' pass (phi_pass) reads them
+    int phi_pass;
+    void* wbuf;
 };
 
 // A Launch with every field cleared and no test hook armed.
@@ -994,8 +1031,10 @@ static cudaError_t launch(const Launch& L) {
     if (L.DK != HD || L.DV != HD || L.chunk != CS) return cudaErrorInvalidValue;
     if (L.HQK <= 0 || L.HV <= 0 || L.HV % L.HQK != 0) return cudaErrorInvalidValue;
     if (L.T < 0 || L.nseq < 0 || L.HV > 65535 || L.nseq > 65535) return cudaErrorInvalidValue;
-    if (!L.q || !L.k || !L.v || (!L.out && !L.state_pass) || !L.sf || !L.ws) return cudaErrorInvalidValue;
+    if (!L.q || !L.k || !L.v || (!L.out && !L.state_pass && !L.phi_pass) || !L.sf || !L.ws) return cudaErrorInvalidValue;
     if (L.state_pass && ((L.seg_kernel == 2 && !L.v0) || L.seg_chunks <= 0 || L.s0)) return cudaErrorInvalidValue;
+    if ((L.state_pass || L.phi_pass) && L.seg_kernel == 1 && (!L.wbuf || !aligned16(L.wbuf))) return cudaErrorInvalidValue;
+    if (L.phi_pass && (L.seg_kernel != 1 || L.state_pass || L.s0 || L.seg_chunks <= 0)) return cudaErrorInvalidValue;
     if (L.prestage ? (!L.ga || !L.gb || !L.A_log || !L.dt_bias) : (!L.g || !L.beta)) return cudaErrorInvalidValue;
     if (L.ws_bytes < WS_HEADER) return cudaErrorInvalidValue;
     const bool gated = (L.z != nullptr) || (L.w != nullptr);
@@ -1043,10 +1082,11 @@ static cudaError_t launch(const Launch& L) {
     p.seg_chunks = L.seg_chunks;
     p.seg_per_seq = L.seg_per_seq;
     p.sf_last_only = L.sf_last_only;
+    p.wbuf = static_cast<uint8_t*>(L.wbuf);
     p.tm_v0 = p.tm_v;
     if (L.seg_chunks > 0) {  // segmented passes (the caller checked that the chosen kernel can run)
         if (L.dbg || L.prestage || L.cu || L.nseq != L.B * L.seg_per_seq) return cudaErrorInvalidValue;
-        if (L.state_pass && gated) return cudaErrorInvalidValue;
+        if ((L.state_pass || L.phi_pass) && gated) return cudaErrorInvalidValue;
         if (L.seg_kernel == 2) {
             if (L.state_pass && !make_map(&p.tm_v0, L.v0, 1, CS, 1)) return cudaErrorInvalidValue;  // one zero tile
             return launch_split(p, L.nseq, L.state_pass ? 2 * L.HV : L.HV, L.stream);
@@ -1061,7 +1101,7 @@ static cudaError_t launch(const Launch& L) {
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(1, L.seg_chunks > 0 && L.state_pass ? 2 * L.HV : L.HV, L.nseq);
+    cfg.gridDim = dim3(1, L.HV, L.nseq);
     cfg.blockDim = dim3(NTHREADS, 1, 1);
     cfg.dynamicSmemBytes = SMEM_ALLOC;
     cfg.stream = L.stream;
@@ -1074,7 +1114,9 @@ static cudaError_t launch(const Launch& L) {
     void (*kernel)(Params) = L.prestage ? (L.dbg ? gdn_prefill_kernel<true, true> : gdn_prefill_kernel<true, false>)
                                         : (L.dbg ? gdn_prefill_kernel<false, true> : gdn_prefill_kernel<false, false>);
     if (L.seg_chunks > 0)
-        kernel = L.state_pass ? gdn_prefill_kernel<false, false, SEG_STATE> : gdn_prefill_kernel<false, false, SEG_OUTPUT>;
+        kernel = L.state_pass ? gdn_prefill_kernel<false, false, SEG_STATE>
+                              : (L.phi_pass ? gdn_prefill_kernel<false, false, SEG_PHI>
+                                            : gdn_prefill_kernel<false, false, SEG_OUTPUT>);
     e = cudaLaunchKernelEx(&cfg, kernel, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
@@ -1116,18 +1158,23 @@ constexpr size_t SEG_ZERO_BYTES = (size_t)CS * HD * 2;  // one zero bf16 tile [6
 // Plan of a segmented call: segments per sequence, chunks per segment and the kernel that runs
 // the passes (1: one CTA per (segment, head), 2: cluster split), from a wave model of B200
 // measurements. A wave of units costs its chunk count plus a start-up and drain overhead, times
-// the kernel's chunk period; the call costs the state pass (2 U s units: the zero-state and the
-// identity runs), the scan (one step per segment) and the output pass (U s units), U = B HV.
+// the kernel's chunk period; the call costs the state pass (the zero-state and the identity runs
+// of every segment but the last, U (s - 1) units each), the scan (one step per segment) and the
+// output pass (U s units), U = B HV.
 //   cluster split: 4 SMs per unit, clusters per wave from the occupancy API (32 on B200: clusters
-//     must fit inside a GPC), ~3.0 us per chunk in either pass, ~5 periods of overhead;
-//   one CTA per unit: one unit per SM, ~10.2 us per chunk in the output pass, ~6 us in the state
-//     pass (no output products, norm or q loads), ~1 period of overhead.
+//     must fit inside a GPC), ~3.0 us per chunk in either pass (both runs in one grid), ~5 periods
+//     of overhead;
+//   one CTA per unit: one unit per SM, ~10.2 us per chunk in the output pass, ~7.4 us in the
+//     zero-state runs (no output products, norm or q loads) and ~3.2 us in the identity runs' pass
+//     (no chunk preparation: it reads the zero-state runs' W), ~1 period of overhead;
+//   the scan ~1.7 us per step.
 // One pass (s = 1) costs what the plain call launches. The cheapest plan wins, fewer segments on
 // ties. GDN_B200_KERNEL=fused|split restricts the passes to one kernel.
 struct SegPlan {
     int nseg, per, kernel;
 };
-constexpr double SPLIT_CHUNK_US = 3.0, FUSED_CHUNK_US = 10.2, STATE_CHUNK_US = 6.0, SCAN_STEP_US = 1.0;
+constexpr double SPLIT_CHUNK_US = 3.0, FUSED_CHUNK_US = 10.2, STATE_CHUNK_US = 7.4, PHI_CHUNK_US = 3.2,
+                 SCAN_STEP_US = 1.7;
 constexpr int WAVE_OVERHEAD = 5, FUSED_OVERHEAD = 1;
 static SegPlan plan_segments(int B, int HV, int NC, int segments, int sms, int cluster_wave, bool split_ok,
                              bool fused_ok) {
@@ -1137,11 +1184,11 @@ static SegPlan plan_segments(int B, int HV, int NC, int segments, int sms, int c
     if (!split_ok) fused_ok = true;  // the one-CTA kernel always runs
     auto cost = [&](int eff, int per, int kernel) {  // segmented call, `eff` segments of `per` chunks
         const double scan = eff * SCAN_STEP_US;
-        const long long su = 2 * U * (eff - 1);  // state-pass units: every segment but the last, twice
+        const long long su = U * (eff - 1);  // units of either run kind: every segment but the last
         if (kernel == 2)
-            return (waves(su, cluster_wave) + waves(U * eff, cluster_wave)) * (per + WAVE_OVERHEAD) * SPLIT_CHUNK_US +
-                   scan;
-        return waves(su, sms) * (per + FUSED_OVERHEAD) * STATE_CHUNK_US +
+            return (waves(2 * su, cluster_wave) + waves(U * eff, cluster_wave)) * (per + WAVE_OVERHEAD) *
+                       SPLIT_CHUNK_US + scan;
+        return waves(su, sms) * (per + FUSED_OVERHEAD) * (STATE_CHUNK_US + PHI_CHUNK_US) +
                waves(U * eff, sms) * (per + FUSED_OVERHEAD) * FUSED_CHUNK_US + scan;
     };
     auto cheaper_kernel = [&](int eff, int per) {
@@ -1193,10 +1240,17 @@ static SegPlan resolve_segments(int B, int T, int HV, int segments) {
 }
 
 // status header, the zero tile, the state pass's maps A_j and PhiT_j of every segment but the
-// last ([B (nseg - 1)][2 HV][128][128] fp32) and the entry states ([B nseg][HV][128][128] fp32)
-static size_t segmented_bytes(int B, int HV, int nseg) {
-    if (nseg <= 1) return WS_HEADER;
-    return WS_HEADER + SEG_ZERO_BYTES + (size_t)B * (3 * nseg - 2) * HV * HD * HD * sizeof(float);
+// last ([B (nseg - 1)][2 HV][128][128] fp32), the entry states ([B nseg][HV][128][128] fp32) and,
+// for passes on the one-CTA kernel, the W^T tiles of every chunk of those segments
+// ([B (nseg - 1)][HV][per] x 32 KB)
+constexpr size_t W_TILE_BYTES = 32768;
+static size_t seg_maps_bytes(int B, int HV, int nseg) {
+    return (size_t)B * (3 * nseg - 2) * HV * HD * HD * sizeof(float);
+}
+static size_t segmented_bytes(const SegPlan& pl, int B, int HV) {
+    if (pl.nseg <= 1) return WS_HEADER;
+    const size_t w = pl.kernel == 1 ? (size_t)B * (pl.nseg - 1) * HV * pl.per * W_TILE_BYTES : 0;
+    return WS_HEADER + SEG_ZERO_BYTES + seg_maps_bytes(B, HV, pl.nseg) + w;
 }
 
 static size_t debug_bytes(int B, int T, int HV) {
@@ -1219,7 +1273,7 @@ size_t deltanet_prefill_workspace_size(int B, int T, int HV, int DK, int DV, int
 size_t deltanet_segmented_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size, int segments) {
     (void)DK; (void)DV; (void)chunk_size;
     if (B <= 0 || T <= 0 || HV <= 0) return gdn::WS_HEADER;
-    return gdn::segmented_bytes(B, HV, gdn::resolve_segments(B, T, HV, segments).nseg);
+    return gdn::segmented_bytes(gdn::resolve_segments(B, T, HV, segments), B, HV);
 }
 
 // The plan deltanet_chunk_prefill_segmented makes for these sizes on the current device: segments
@@ -1374,7 +1428,7 @@ cudaError_t deltanet_chunk_prefill_segmented(const void* q, const void* k, const
                                                 HV, HQK, DK, DV, chunk_size, workspace, workspace_bytes, stream)
                  : deltanet_chunk_prefill(q, k, v, g, beta, out, initial_state, final_state, B, T, HV, HQK, DK, DV,
                                           chunk_size, workspace, workspace_bytes, stream, 0);
-    if (!workspace || workspace_bytes < gdn::segmented_bytes(B, HV, nseg)) return cudaErrorInvalidValue;
+    if (!workspace || workspace_bytes < gdn::segmented_bytes(plan, B, HV)) return cudaErrorInvalidValue;
     char* ws = static_cast<char*>(workspace);
     void* zero = ws + gdn::WS_HEADER;
     float* stt = reinterpret_cast<float*>(ws + gdn::WS_HEADER + gdn::SEG_ZERO_BYTES);  // [B (nseg-1)][2 HV][D][D]
@@ -1388,11 +1442,20 @@ cudaError_t deltanet_chunk_prefill_segmented(const void* q, const void* k, const
     L.ws = workspace; L.ws_bytes = workspace_bytes; L.stream = stream;
     L.seg_chunks = per; L.seg_kernel = plan.kernel;
     // state pass over the first nseg - 1 segments of each sequence (the last one's maps are not
-    // needed): A_j (zero entry, v) at heads [0, HV), PhiT_j (identity entry, zero v) at [HV, 2 HV)
+    // needed): A_j (zero entry, v) at heads [0, HV), PhiT_j (identity entry, zero v) at [HV, 2 HV).
+    // The cluster-split kernel runs both in one grid; the one-CTA kernel runs the zero-state runs,
+    // which store every chunk's W^T tiles, then the identity runs, which read them.
     L.nseq = B * (nseg - 1); L.seg_per_seq = nseg - 1;
     L.state_pass = 1; L.v0 = zero; L.sf = stt; L.out = nullptr;
+    if (plan.kernel == 1) L.wbuf = ws + gdn::WS_HEADER + gdn::SEG_ZERO_BYTES + gdn::seg_maps_bytes(B, HV, nseg);
     e = gdn::launch(L);
     if (e != cudaSuccess) return e;
+    if (plan.kernel == 1) {
+        L.state_pass = 0; L.phi_pass = 1; L.v0 = nullptr;
+        e = gdn::launch(L);
+        if (e != cudaSuccess) return e;
+        L.phi_pass = 0; L.wbuf = nullptr;
+    }
     e = gdn::launch_segment_scan(stt, initial_state, entry, B, HV, nseg, stream);
     if (e != cudaSuccess) return e;
     // output pass over every segment from its entry state; the last segment's final state is the sequence's

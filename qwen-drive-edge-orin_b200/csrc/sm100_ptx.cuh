@@ -135,6 +135,24 @@ __device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32
         : "memory");
 }
 
+// Bulk copy of `bytes` contiguous bytes global -> this CTA's shared memory, completing on `bar`
+// (both addresses 16-byte aligned, bytes a multiple of 16). No multicast.
+__device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Bulk copy this CTA's shared memory -> global (a bulk group of the issuing thread), and the
+// waits of the issuing thread for its groups: reads of the source done / copies complete.
+__device__ __forceinline__ void bulk_store_s2g(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(src), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 // 4-D tiled load global -> shared, completion counted on `bar` (bytes).
 // Plain (non-multicast) form only.
