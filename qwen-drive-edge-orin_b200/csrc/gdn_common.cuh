@@ -64,10 +64,12 @@ struct Params {
     // Output pass of a segmented call: only the last segment of each sequence writes its final
     // state, at sf[b] (the other segments' final states are the next segments' entry states).
     int sf_last_only;
-    // One-CTA kernel's segmented state passes: W^T hi/lo of every chunk of every (segment, head),
-    // 32 KB each in the shared-memory tile layout, written by the zero-state runs and read by the
-    // identity runs' pass (which then forms no chunk preparation of its own).
+    // One-CTA kernel's segmented passes: a record of T' and W^T hi/lo tiles (48 KB, the
+    // shared-memory tile layout) per chunk of every (sequence, segment, head), written by the
+    // zero-state runs and read by the identity runs and the output pass (which then form no
+    // triangular inverse of their own); seg_total = segments per sequence (record indexing).
     uint8_t* wbuf;
+    int seg_total;
 };
 
 // Byte offset of bf16 element (row, col) in a 128B-swizzled tile whose panels

@@ -89,6 +89,10 @@ constexpr uint32_t MISC_FLAG = 1108;
 constexpr uint32_t MISC_W = 1152;   // norm weight [128] f32
 constexpr uint32_t MISC_BYTES = 1664;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
+// A record of the segmented passes' workspace: one chunk's T' hi/lo (the 16 KB at OFF_TP_HI) and
+// W^T hi/lo (the 32 KB at OFF_W_HI), byte for byte.
+constexpr uint32_t WREC_BYTES = 16384 + 32768;
+static_assert(OFF_TP_LO == OFF_TP_HI + 8192 && OFF_W_LO == OFF_W_HI + 16384, "a record is two contiguous tiles");
 constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;  // slack for manual 1024 alignment
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB per-block shared memory limit");
 
@@ -111,7 +115,7 @@ constexpr uint32_t TM_SA_LO = 448;
 // let the state update start while the output products still run: BAR_DS = dS, BAR_O1 = S^T q^T,
 // BAR_O2 = v_new^T M^T, issued by thread 32 once thread 0 has issued dS and arrived on BAR_DSI).
 enum { BAR_Q = 0, BAR_K = 1, BAR_V = 2, BAR_Z = 3, BAR_MMA = 4, BAR_DS = 5, BAR_O1 = 6, BAR_O2 = 7, BAR_DSI = 8,
-       NBAR = 9 };
+       BAR_W = 9 /* segmented output pass: T' and W^T tiles from the state pass */, NBAR = 10 };
 static_assert(MISC_BAR + 8 * NBAR <= MISC_TMEM, "barriers overlap the TMEM address word");
 
 
@@ -124,25 +128,31 @@ constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192
 // (the kernel is sensitive to instruction fetch; its loop body is larger than an SM's
 // instruction cache). So are the passes of a segmented call (kSeg, below).
 //
-// kSeg = SEG_OUTPUT: output pass of a segmented call. Block z indexes (sequence b, segment j) =
-//   (z / seg_per_seq, z % seg_per_seq), covering tokens [j seg_chunks 64, min((j+1) seg_chunks 64, T))
-//   of batch row b, from the entry state s0[z]; only the last segment of each sequence writes its
-//   final state, at sf[b].
-// kSeg = SEG_STATE: state pass, the zero-state runs. The same segments (every one but the last),
-//   grid y = HV: v-head y from a zero state (s0 null); writes its final state A at sf[z][y] of the
-//   [z][2 HV] map array, and every chunk's W^T hi/lo tiles to wbuf. Nothing else is formed: no q
-//   load, no M, no output products, no norm.
-// kSeg = SEG_PHI: the identity runs' pass, after it: v-head y from the identity with v = 0. Its
-//   chunk update needs only W (from wbuf), k and the gates, so it forms no chunk preparation (no
-//   P1, L, inverse, T', P3) and loads no q or v; k alternates between the two halves of the
-//   [q; k] panels so that the next chunk's k loads a chunk ahead. Writes its final state, the map
-//   Phi, transposed (the layout the entry-state scan reads) at sf[z][HV + y].
+// The passes of a segmented call. Block z indexes (sequence b, segment j) = (z / seg_per_seq,
+// z % seg_per_seq), covering tokens [j seg_chunks 64, min((j+1) seg_chunks 64, T)) of batch row b;
+// grid y = HV. A record of wbuf holds the T' and W^T hi/lo tiles of one chunk of one (sequence,
+// segment, head) as the zero-state run formed them (48 KB, the shared-memory tile layout), indexed
+// by (b, j, head, chunk) with seg_total segments per sequence.
+// kSeg = SEG_STATE: the zero-state runs of every segment: v-head y from a zero state (s0 null).
+//   Stores every chunk's record, and (but the last segment) its final state A at [b (seg_total-1)
+//   + j][y] of the [.][2 HV] map array sf. Nothing else is formed: no q load, no M, no output
+//   products, no norm.
+// kSeg = SEG_PHI: the identity runs of every segment but the last (seg_per_seq = seg_total - 1):
+//   v-head y from the identity with v = 0. Its chunk update needs only W (from the record), k and
+//   the gates, so it forms no chunk preparation (no P1, L, inverse, T', P3) and loads no q or v; k
+//   alternates between the two halves of the [q; k] panels so that the next chunk's k loads a
+//   chunk ahead. Writes its final state, the map Phi, transposed (the layout the entry-state scan
+//   reads) at [z][HV + y] of sf.
+// kSeg = SEG_OUTPUT: every segment from its entry state s0[z], with the full outputs; it forms M
+//   (P1) but takes T' and W^T from the records (no L, inverse, T'/T'' split or P3). Only the last
+//   segment of each sequence writes its final state, at sf[b].
 constexpr int SEG_NONE = 0, SEG_OUTPUT = 1, SEG_STATE = 2, SEG_PHI = 3;
 template <bool kPrestage, bool kDebug, int kSeg = SEG_NONE>
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
     constexpr bool kState = (kSeg == SEG_STATE);
     constexpr bool kPhi = (kSeg == SEG_PHI);
     constexpr bool kLean = kState || kPhi;  // no q, M, output products or norm
+    constexpr bool kPrepped = (kSeg == SEG_OUTPUT);  // T' and W^T from the zero-state runs' records
     // identity run (v = 0, identity entry state)
     constexpr bool phi_unit = kPhi;
     // the tensor maps are kernel parameters, not data of the previous launch: fetch them while it ends
@@ -259,14 +269,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::tma_load_4d(sb + OFF_QK + koff(n), &p.tm_k, bar(BAR_K), 0, hq, t, bcoord);
         ptx::tma_load_4d(sb + OFF_QK + 16384 + koff(n), &p.tm_k, bar(BAR_K), 64, hq, t, bcoord);
     };
-    // W^T hi/lo tiles of chunk n in wbuf, and (identity-run pass) the two shared-memory buffers they
-    // are loaded into (the T'/T'' area is free there); the v barrier counts those loads
-    auto wofs = [&](int n) -> size_t { return ((size_t)(seq * p.HV + h) * p.seg_chunks + n) * 32768; };
+    // Chunk n's record in wbuf: T' hi/lo (16 KB) then W^T hi/lo (32 KB). The identity-run pass loads
+    // W^T into two alternating shared-memory buffers (the T'/T'' area is free there; the v barrier
+    // counts those loads); the output pass loads both into their own places (barrier W).
+    const int seg_j = kSeg != SEG_NONE ? seq - bcoord * p.seg_per_seq : 0;
+    auto wrec = [&](int n) -> size_t {
+        return ((((size_t)bcoord * p.seg_total + seg_j) * p.HV + h) * p.seg_chunks + n) * WREC_BYTES;
+    };
     auto wtile = [](int n) -> uint32_t { return (n & 1) ? OFF_X : OFF_W_HI; };
     auto load_w = [&](int n) {
         ++issued[BAR_V];
         ptx::mbar_arrive_expect_tx(bar(BAR_V), 32768);
-        ptx::bulk_load_g2s(sb + wtile(n), p.wbuf + wofs(n), 32768, bar(BAR_V));
+        ptx::bulk_load_g2s(sb + wtile(n), p.wbuf + wrec(n) + 16384, 32768, bar(BAR_V));
+    };
+    auto load_tw = [&](int n) {
+        ++issued[BAR_W];
+        ptx::mbar_arrive_expect_tx(bar(BAR_W), WREC_BYTES);
+        ptx::bulk_load_g2s(sb + OFF_TP_HI, p.wbuf + wrec(n), 16384, bar(BAR_W));
+        ptx::bulk_load_g2s(sb + OFF_W_HI, p.wbuf + wrec(n) + 16384, 32768, bar(BAR_W));
     };
     auto load_v = [&](int n) {
         ++issued[BAR_V];
@@ -312,6 +332,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         load_k(0);
         if (p.withhold_v_chunk != 0 && !phi_unit) load_v(0);
         if (kPhi) load_w(0);
+        if (kPrepped) load_tw(0);
     }
     if (tid == 128 && NC > 0 && p.gated) load_z(0);  // z feeds the gate product (while C12 runs)
     // Gate inputs of the next chunk are prefetched into warp 1's registers (lane l: tokens 2l,
@@ -477,7 +498,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                     put8_split(sb + OFF_M_HI + co, sb + OFF_M_LO + co, m + 8 * ch, true);
                 }
               }
-            } else {  // L row i: beta_i k_i.k_j e^{c_i - c_j}, j < i
+            } else if (!kPrepped) {  // L row i: beta_i k_i.k_j e^{c_i - c_j}, j < i
                 const int i = row - CS;
                 const float ci = c_s[i], bi = beta_s[i];
                 float* lrow = Ls + i * LSTRIDE + 32 * half;
@@ -494,9 +515,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 }
             }
         }
+        if (kState && tid == 0 && n > 0) ptx::bulk_wait_read_all();  // the last record's stores have read T', W^T
         ptx::tc_fence_before();
         __syncthreads();
-
+        if constexpr (kPrepped) {
+            // ---- this chunk's T' and W^T as the zero-state run formed them; the v^T T'^T part of C12 ----
+            wait_bar(BAR_V, ph);
+            wait_bar(BAR_W, ph);
+            ptx::fence_proxy_async_smem();  // the M tiles, before the async proxy reads them
+            __syncthreads();
+            if (*abort_flag) break;
+            if (tid == 0) {
+                ptx::tc_fence_after();
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const uint64_t a = desc(dlo8k, OFF_V + s * 2048);
+                    const uint64_t b = desc(dlo16, OFF_TP_HI + s * 32);
+                    ptx::mma_bf16(tmem + TM_C12, a, b, ID_U, s > 0);
+                }
+            }
+        } else {
         // ---- T = (I + L)^-1 (fp32, CUDA cores) ----
         invert_unit_lower<true>(Ls, X, tid, [](int) {}, [] { __syncthreads(); });
         if (rec) {
@@ -541,7 +579,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
                 st_shared_v4(a, w4[0], w4[1], w4[2], w4[3]);
             }
         }
-        if (kState && tid == 0 && n > 0) ptx::bulk_wait_read_all();  // the W^T tiles' store has read them
         ptx::fence_proxy_async_smem();
         __syncthreads();
 
@@ -590,7 +627,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         ptx::fence_proxy_async_smem();
         __syncthreads();
         if (*abort_flag) break;
-        if (kState && tid == 0) ptx::bulk_store_s2g(p.wbuf + wofs(n), sb + OFF_W_HI, 32768);  // for the identity runs
+        if (kState && tid == 0) {  // this chunk's record, for the identity runs and the output pass
+            ptx::bulk_store_s2g(p.wbuf + wrec(n), sb + OFF_TP_HI, 16384);
+            ptx::bulk_store_s2g(p.wbuf + wrec(n) + 16384, sb + OFF_W_HI, 32768);
+        }
+        }  // inverse, T' / T'', P3 and W^T
         }  // chunk preparation
 
         // ---- C12: v_new^T = v^T T'^T - S^T W^T (the v^T T'^T part was issued with P3) ----
@@ -644,6 +685,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
         if (tid == 0 && n + 1 < NC && n + 1 != p.withhold_v_chunk && !phi_unit && !*abort_flag)
             load_v(n + 1);  // v tile consumed
         if (kPhi && tid == 0 && n + 1 < NC && !*abort_flag) load_w(n + 1);  // C12 of chunk n - 1 read that buffer
+        if (kPrepped && tid == 0 && n + 1 < NC && !*abort_flag) load_tw(n + 1);  // T' and W^T are read (C12 done)
         {   // v_new^T (fp32, cols TM_C12) -> hi/lo bf16 pairs of v_new and v_new e^{cL-c} (TMEM A operands)
             float v[32];
             {
@@ -857,11 +899,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     //      output pass only the last segment's, at (batch row, h) ----
     if (!*abort_flag) {
         float* sfp = p.sf + ((size_t)seq * p.HV + h) * HD * HD;
-        if (kLean) sfp = p.sf + ((size_t)seq * 2 * p.HV + (kPhi ? p.HV : 0) + h) * HD * HD;  // the [z][2 HV] maps
+        if (kLean)  // the [b (seg_total - 1) + j][2 HV] maps; the last segment's zero-state run has none
+            sfp = seg_j < p.seg_total - 1
+                      ? p.sf + (((size_t)bcoord * (p.seg_total - 1) + seg_j) * 2 * p.HV + (kPhi ? p.HV : 0) + h) * HD * HD
+                      : nullptr;
         if (kSeg == SEG_OUTPUT)
             sfp = (seq % p.seg_per_seq == p.seg_per_seq - 1) ? p.sf + ((size_t)(seq / p.seg_per_seq) * p.HV + h) * HD * HD
                                                             : nullptr;
-        if (phi_unit) {  // the map Phi is stored transposed, PhiT[k][i] = Phi[i][k] (k = row): the scan's layout
+        if (phi_unit && sfp != nullptr) {  // the map Phi is stored transposed, PhiT[k][i] = Phi[i][k] (k = row): the scan's layout
             float4* dst = reinterpret_cast<float4*>(sfp + (size_t)row * HD + 64 * half);
 #pragma unroll
             for (int j = 0; j < 16; ++j) dst[j] = make_float4(S[4 * j], S[4 * j + 1], S[4 * j + 2], S[4 * j + 3]);
@@ -873,7 +918,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
             }
         }
     }
-    if (kState && tid == 0) ptx::bulk_wait_all();  // the W^T tiles' stores have completed
+    if (kState && tid == 0) ptx::bulk_wait_all();  // the records' stores have completed
     // Abort path: wait (bounded) for this CTA's own TMA copies and MMAs still
     // in flight before its shared memory and TMEM are released.
     if (*abort_flag && (tid == 0 || tid == 32 || tid == 128)) {
@@ -1017,6 +1062,7 @@ struct Launch {
     // identity runs' pass (phi_pass) reads them
     int phi_pass;
     void* wbuf;
+    int seg_total;  // segments per sequence of the whole call (record and map indexing)
 };
 
 // A Launch with every field cleared and no test hook armed.
@@ -1033,7 +1079,7 @@ static cudaError_t launch(const Launch& L) {
     if (L.T < 0 || L.nseq < 0 || L.HV > 65535 || L.nseq > 65535) return cudaErrorInvalidValue;
     if (!L.q || !L.k || !L.v || (!L.out && !L.state_pass && !L.phi_pass) || !L.sf || !L.ws) return cudaErrorInvalidValue;
     if (L.state_pass && ((L.seg_kernel == 2 && !L.v0) || L.seg_chunks <= 0 || L.s0)) return cudaErrorInvalidValue;
-    if ((L.state_pass || L.phi_pass) && L.seg_kernel == 1 && (!L.wbuf || !aligned16(L.wbuf))) return cudaErrorInvalidValue;
+    if (L.seg_chunks > 0 && L.seg_kernel == 1 && (!L.wbuf || !aligned16(L.wbuf) || L.seg_total < 2)) return cudaErrorInvalidValue;
     if (L.phi_pass && (L.seg_kernel != 1 || L.state_pass || L.s0 || L.seg_chunks <= 0)) return cudaErrorInvalidValue;
     if (L.prestage ? (!L.ga || !L.gb || !L.A_log || !L.dt_bias) : (!L.g || !L.beta)) return cudaErrorInvalidValue;
     if (L.ws_bytes < WS_HEADER) return cudaErrorInvalidValue;
@@ -1083,6 +1129,7 @@ static cudaError_t launch(const Launch& L) {
     p.seg_per_seq = L.seg_per_seq;
     p.sf_last_only = L.sf_last_only;
     p.wbuf = static_cast<uint8_t*>(L.wbuf);
+    p.seg_total = L.seg_total;
     p.tm_v0 = p.tm_v;
     if (L.seg_chunks > 0) {  // segmented passes (the caller checked that the chosen kernel can run)
         if (L.dbg || L.prestage || L.cu || L.nseq != L.B * L.seg_per_seq) return cudaErrorInvalidValue;
@@ -1164,9 +1211,10 @@ constexpr size_t SEG_ZERO_BYTES = (size_t)CS * HD * 2;  // one zero bf16 tile [6
 //   cluster split: 4 SMs per unit, clusters per wave from the occupancy API (32 on B200: clusters
 //     must fit inside a GPC), ~3.0 us per chunk in either pass (both runs in one grid), ~5 periods
 //     of overhead;
-//   one CTA per unit: one unit per SM, ~10.2 us per chunk in the output pass, ~7.4 us in the
-//     zero-state runs (no output products, norm or q loads) and ~3.2 us in the identity runs' pass
-//     (no chunk preparation: it reads the zero-state runs' W), ~1 period of overhead;
+//   one CTA per unit: one unit per SM; the zero-state runs of every segment (~7.4 us per chunk:
+//     no output products, norm or q loads), the identity runs (~3.2 us: no chunk preparation, they
+//     read the zero-state runs' W) and the output pass (~7.5 us: it reads their T' and W), ~1
+//     period of overhead; one pass of the one-CTA kernel costs ~10.2 us per chunk;
 //   the scan ~1.7 us per step.
 // One pass (s = 1) costs what the plain call launches. The cheapest plan wins, fewer segments on
 // ties. GDN_B200_KERNEL=fused|split restricts the passes to one kernel.
@@ -1174,7 +1222,7 @@ struct SegPlan {
     int nseg, per, kernel;
 };
 constexpr double SPLIT_CHUNK_US = 3.0, FUSED_CHUNK_US = 10.2, STATE_CHUNK_US = 7.4, PHI_CHUNK_US = 3.2,
-                 SCAN_STEP_US = 1.7;
+                 OUTPUT_CHUNK_US = 7.5, SCAN_STEP_US = 1.7;
 constexpr int WAVE_OVERHEAD = 5, FUSED_OVERHEAD = 1;
 static SegPlan plan_segments(int B, int HV, int NC, int segments, int sms, int cluster_wave, bool split_ok,
                              bool fused_ok) {
@@ -1188,8 +1236,8 @@ static SegPlan plan_segments(int B, int HV, int NC, int segments, int sms, int c
         if (kernel == 2)
             return (waves(2 * su, cluster_wave) + waves(U * eff, cluster_wave)) * (per + WAVE_OVERHEAD) *
                        SPLIT_CHUNK_US + scan;
-        return waves(su, sms) * (per + FUSED_OVERHEAD) * (STATE_CHUNK_US + PHI_CHUNK_US) +
-               waves(U * eff, sms) * (per + FUSED_OVERHEAD) * FUSED_CHUNK_US + scan;
+        return (waves(U * eff, sms) * (STATE_CHUNK_US + OUTPUT_CHUNK_US) + waves(su, sms) * PHI_CHUNK_US) *
+                   (per + FUSED_OVERHEAD) + scan;
     };
     auto cheaper_kernel = [&](int eff, int per) {
         if (!split_ok) return 1;
@@ -1241,15 +1289,14 @@ static SegPlan resolve_segments(int B, int T, int HV, int segments) {
 
 // status header, the zero tile, the state pass's maps A_j and PhiT_j of every segment but the
 // last ([B (nseg - 1)][2 HV][128][128] fp32), the entry states ([B nseg][HV][128][128] fp32) and,
-// for passes on the one-CTA kernel, the W^T tiles of every chunk of those segments
-// ([B (nseg - 1)][HV][per] x 32 KB)
-constexpr size_t W_TILE_BYTES = 32768;
+// for passes on the one-CTA kernel, the records (T' and W^T tiles) of every chunk of every
+// segment ([B nseg][HV][per] x 48 KB)
 static size_t seg_maps_bytes(int B, int HV, int nseg) {
     return (size_t)B * (3 * nseg - 2) * HV * HD * HD * sizeof(float);
 }
 static size_t segmented_bytes(const SegPlan& pl, int B, int HV) {
     if (pl.nseg <= 1) return WS_HEADER;
-    const size_t w = pl.kernel == 1 ? (size_t)B * (pl.nseg - 1) * HV * pl.per * W_TILE_BYTES : 0;
+    const size_t w = pl.kernel == 1 ? (size_t)B * pl.nseg * HV * pl.per * WREC_BYTES : 0;
     return WS_HEADER + SEG_ZERO_BYTES + seg_maps_bytes(B, HV, pl.nseg) + w;
 }
 
@@ -1440,21 +1487,27 @@ cudaError_t deltanet_chunk_prefill_segmented(const void* q, const void* k, const
     L.B = B; L.T = T; L.HV = HV; L.HQK = HQK; L.DK = DK; L.DV = DV; L.chunk = chunk_size;
     L.max_nc = per;
     L.ws = workspace; L.ws_bytes = workspace_bytes; L.stream = stream;
-    L.seg_chunks = per; L.seg_kernel = plan.kernel;
-    // state pass over the first nseg - 1 segments of each sequence (the last one's maps are not
-    // needed): A_j (zero entry, v) at heads [0, HV), PhiT_j (identity entry, zero v) at [HV, 2 HV).
-    // The cluster-split kernel runs both in one grid; the one-CTA kernel runs the zero-state runs,
-    // which store every chunk's W^T tiles, then the identity runs, which read them.
-    L.nseq = B * (nseg - 1); L.seg_per_seq = nseg - 1;
+    L.seg_chunks = per; L.seg_kernel = plan.kernel; L.seg_total = nseg;
+    // State pass: the maps A_j (zero entry, v) at heads [0, HV) and PhiT_j (identity entry, zero v)
+    // at [HV, 2 HV) of the segments but the last (whose maps are not needed). The cluster-split
+    // kernel runs both in one grid over those segments. The one-CTA kernel runs the zero-state runs
+    // of every segment, which store every chunk's record (T' and W^T), then the identity runs,
+    // which read W^T from them; the output pass reads T' and W^T from them too.
     L.state_pass = 1; L.v0 = zero; L.sf = stt; L.out = nullptr;
-    if (plan.kernel == 1) L.wbuf = ws + gdn::WS_HEADER + gdn::SEG_ZERO_BYTES + gdn::seg_maps_bytes(B, HV, nseg);
-    e = gdn::launch(L);
-    if (e != cudaSuccess) return e;
     if (plan.kernel == 1) {
-        L.state_pass = 0; L.phi_pass = 1; L.v0 = nullptr;
+        L.wbuf = ws + gdn::WS_HEADER + gdn::SEG_ZERO_BYTES + gdn::seg_maps_bytes(B, HV, nseg);
+        L.nseq = B * nseg; L.seg_per_seq = nseg;
         e = gdn::launch(L);
         if (e != cudaSuccess) return e;
-        L.phi_pass = 0; L.wbuf = nullptr;
+        L.state_pass = 0; L.phi_pass = 1; L.v0 = nullptr;
+        L.nseq = B * (nseg - 1); L.seg_per_seq = nseg - 1;
+        e = gdn::launch(L);
+        if (e != cudaSuccess) return e;
+        L.phi_pass = 0;
+    } else {
+        L.nseq = B * (nseg - 1); L.seg_per_seq = nseg - 1;
+        e = gdn::launch(L);
+        if (e != cudaSuccess) return e;
     }
     e = gdn::launch_segment_scan(stt, initial_state, entry, B, HV, nseg, stream);
     if (e != cudaSuccess) return e;

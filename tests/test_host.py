@@ -111,11 +111,11 @@ def test_segmented_workspace_and_argument_checks():
     """deltanet_chunk_prefill_segmented: workspace = status header + one zero tile + the state
     pass's maps A and Phi of every segment but the last ([B (segments - 1), 2 HV, 128, 128] fp32)
     + the entry states ([B segments, HV, 128, 128] fp32) + (passes on the one-CTA kernel, the only
-    kernel without a device) the W^T tiles of every chunk of the state pass (32 KB each); one
-    segment is the plain call's 256 bytes; bad arguments are rejected before any device work."""
+    kernel without a device) a record of T' and W^T tiles per chunk of every segment (48 KB each);
+    one segment is the plain call's 256 bytes; bad arguments are rejected before any device work."""
     lib = gdn_b200.load_library()
     D2 = 128 * 128 * 4
-    ws = lambda B, HV, s, per: 256 + 64 * 128 * 2 + B * (2 * (s - 1) + s) * HV * D2 + B * (s - 1) * HV * per * 32768  # noqa: E731
+    ws = lambda B, HV, s, per: 256 + 64 * 128 * 2 + B * (2 * (s - 1) + s) * HV * D2 + B * s * HV * per * 49152  # noqa: E731
     assert lib.deltanet_segmented_workspace_size(1, 65536, 4, 128, 128, 64, 1) == 256
     assert lib.deltanet_segmented_workspace_size(1, 65536, 4, 128, 128, 64, 9) == ws(1, 4, 9, 114)
     # 1024 chunks in at most 10 segments of 103 chunks: 10 segments
