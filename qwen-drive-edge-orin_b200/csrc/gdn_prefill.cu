@@ -1213,7 +1213,7 @@ constexpr size_t SEG_ZERO_BYTES = (size_t)CS * HD * 2;  // one zero bf16 tile [6
 //     of overhead;
 //   one CTA per unit: one unit per SM; the zero-state runs of every segment (~7.4 us per chunk:
 //     no output products, norm or q loads), the identity runs (~3.2 us: no chunk preparation, they
-//     read the zero-state runs' W) and the output pass (~7.5 us: it reads their T' and W), ~1
+//     read the zero-state runs' W) and the output pass (~7.3 us: it reads their T' and W), ~1
 //     period of overhead; one pass of the one-CTA kernel costs ~10.2 us per chunk;
 //   the scan ~1.7 us per step.
 // One pass (s = 1) costs what the plain call launches. The cheapest plan wins, fewer segments on
@@ -1222,7 +1222,7 @@ struct SegPlan {
     int nseg, per, kernel;
 };
 constexpr double SPLIT_CHUNK_US = 3.0, FUSED_CHUNK_US = 10.2, STATE_CHUNK_US = 7.4, PHI_CHUNK_US = 3.2,
-                 OUTPUT_CHUNK_US = 7.5, SCAN_STEP_US = 1.7;
+                 OUTPUT_CHUNK_US = 7.3, SCAN_STEP_US = 1.7;
 constexpr int WAVE_OVERHEAD = 5, FUSED_OVERHEAD = 1;
 static SegPlan plan_segments(int B, int HV, int NC, int segments, int sms, int cluster_wave, bool split_ok,
                              bool fused_ok) {
