@@ -44,7 +44,11 @@ size_t deltanet_prefill_workspace_size(int B, int T, int HV, int DK, int DV, int
 /* Workspace bytes when dump_debug != 0: the header plus one fp32 record per
  * (b, h, chunk) = [c(64) | T(64x64) | W(64x128) | v_new(64x128) | o(64x128) |
  * S_entry(128x128)]. No counterpart in the reference (its debug dumps are
- * always carried in the workspace, kernels/chunk_delta_cuda.cu:688-697). */
+ * always carried in the workspace, kernels/chunk_delta_cuda.cu:688-697, in its
+ * own carve-out of w | u | de | eg | ed | gl | Sc | M | T | A | T-post-leaf).
+ * The torch binding's chunk_prefill_debug forms the reference's views from
+ * this record (u = W, Sc = S_entry, T, and de / eg / ed / gl from c) and the
+ * inputs (w, M, A, T-post-leaf), in the reference's order and shapes. */
 size_t deltanet_prefill_debug_workspace_size(int B, int T, int HV, int DK, int DV, int chunk_size);
 
 /* Chunked gated delta rule prefill, o written in bf16. Replaces

@@ -126,7 +126,14 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk_size: int = 64, initial_state
     final_state [B, HV, DK, DV] float32). When ``intermediates`` is a dict it
     is filled with per-chunk arrays [B, HV, NC, ...]: ``c`` (in-chunk cumsum),
     ``T`` ((I+L)^-1), ``W`` (k_cumdecay), ``v_new``, ``o`` (fp32, before
-    rounding) and ``S_entry`` (state entering the chunk).
+    rounding) and ``S_entry`` (state entering the chunk); and with the views of
+    the reference's debug entry (``kernels/torch_binding.cpp:57-84``, filled by
+    ``kernels/chunk_delta_cuda.cu``): ``value`` (its ``w`` = T v_beta, :268-282),
+    ``decay`` (its ``de``, :284-294), ``eg`` / ``ed`` / ``gl`` (e^c, e^{c_L - c},
+    e^{c_L}, :284-291), ``A`` (the assembled strict-lower -(k_beta k^T) decay
+    before substitution, :158-175), ``M`` ((q k^T) decay scale, :480-509) and
+    ``T_post_leaf`` (T after the 16 x 16 diagonal leaves are inverted, the other
+    blocks still holding A, :176-214).
 
     Step-by-step restatement of ``kernels/harness/parity_test.py:35-96``:
       * transpose to [B, H, T, D] and pad T to a chunk multiple with zeros (:42-53);
@@ -173,6 +180,16 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk_size: int = 64, initial_state
     decay = np.where(tri_incl, np.exp(np.where(tri_incl, diff, 0.0)), 0.0).astype(f32)
     strict = np.tril(np.ones((C, C), dtype=bool), k=-1)
     attn = np.where(strict, -(k_beta @ np.swapaxes(k, -1, -2)) * decay, 0.0).astype(f32)
+    if intermediates is not None:
+        intermediates["A"] = attn.copy()
+        intermediates["decay"] = decay.copy()
+        intermediates["M"] = ((q @ np.swapaxes(k, -1, -2)) * decay).astype(f32)  # q already carries the scale
+        post = attn.copy()
+        eye16 = np.eye(16, dtype=f32)
+        for bl in range(C // 16):
+            blk = slice(16 * bl, 16 * bl + 16)
+            post[..., blk, blk] = np.linalg.inv(eye16 - attn[..., blk, blk]).astype(f32)
+        intermediates["T_post_leaf"] = post
     for i in range(1, C):
         row = attn[..., i, :i].copy()
         sub = attn[..., :i, :i].copy()
@@ -189,6 +206,10 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk_size: int = 64, initial_state
         intermediates["c"] = c.copy()
         intermediates["T"] = attn.copy()
         intermediates["W"] = k_cumdecay.copy()
+        intermediates["value"] = value.copy()
+        intermediates["eg"] = np.exp(c).astype(f32)
+        intermediates["ed"] = np.exp(c[..., -1:] - c).astype(f32)
+        intermediates["gl"] = np.exp(c[..., -1]).astype(f32)
         intermediates["v_new"] = np.zeros((B, H, NC, C, DV), f32)
         intermediates["S_entry"] = np.zeros((B, H, NC, DK, DV), f32)
     for n in range(NC):

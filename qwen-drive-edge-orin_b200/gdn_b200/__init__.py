@@ -19,6 +19,7 @@ from ``csrc/``; there is no CPU or library fallback.
 from .binding import (  # noqa: F401
     chunk_prefill,
     chunk_prefill_debug,
+    chunk_prefill_debug_native,
     chunk_prefill_gated,
     chunk_prefill_varlen,
     chunk_prefill_segmented,

@@ -4,9 +4,9 @@ Mirrors the reference's pybind wrapper ``kernels/torch_binding.cpp``:
 ``chunk_prefill(q, k, v, g, beta, s0=None) -> [o, sf]`` with the same input
 checks (:89-101: CUDA tensors, bf16 q/k/v, fp32 g/beta, ranks 4/4/3), the same
 s0 handling (:45-48: converted to contiguous fp32) and an error raised on any
-non-success return (:55). ``chunk_prefill_debug`` returns the per-chunk
-intermediates like the reference's debug entry (:57-84), in this kernel's own
-record layout. Calls go through ctypes to ``libgdn_b200.so`` on torch's current
+non-success return (:55). ``chunk_prefill_debug`` returns the reference debug
+entry's list of per-chunk views (:57-84); ``chunk_prefill_debug_native`` this
+kernel's own records. Calls go through ctypes to ``libgdn_b200.so`` on torch's current
 CUDA stream; outputs and the workspace are allocated with torch.
 """
 from __future__ import annotations
@@ -18,7 +18,7 @@ import torch
 
 from ._lib import cuda_error_string, load_library
 
-__all__ = ["chunk_prefill", "chunk_prefill_debug", "chunk_prefill_gated", "chunk_prefill_varlen",
+__all__ = ["chunk_prefill", "chunk_prefill_debug", "chunk_prefill_debug_native", "chunk_prefill_gated", "chunk_prefill_varlen",
            "run_chunk_prefill", "recurrent_decode", "gated_rmsnorm", "chunk_gated_delta_rule_fast", "workspace_size", "GdnError", "read_status"]
 
 CHUNK = 64
@@ -161,15 +161,63 @@ def chunk_prefill(q, k, v, g, beta, s0=None):
     return _run_prefill(q, k, v, g, beta, s0, debug=False)
 
 
-def chunk_prefill_debug(q, k, v, g, beta, s0=None):
-    """[o, sf, c, T, W, v_new, o_fp32, S_entry]: per-chunk intermediates, each [B, HV, NC, ...].
+def chunk_prefill_debug_native(q, k, v, g, beta, s0=None):
+    """[o, sf, c, T, W, v_new, o_fp32, S_entry]: this kernel's per-chunk intermediates, each [B, HV, NC, ...].
 
-    The reference's debug entry (kernels/torch_binding.cpp:119-124) exposes its
-    scratch views; this kernel keeps intermediates on chip, so the debug call
-    asks it to dump them: in-chunk cumsum c, T = (I+L)^-1, W = T diag(beta e^c) K,
-    v_new = U - W S, o before rounding, and the chunk-entry state.
+    The kernel keeps its intermediates on chip; with the debug flag it dumps them: in-chunk
+    cumsum c, T = (I+L)^-1, W = T diag(beta e^c) K, v_new = U - W S, o before rounding, and the
+    chunk-entry state.
     """
     return _run_prefill(q, k, v, g, beta, s0, debug=True)
+
+
+def chunk_prefill_debug(q, k, v, g, beta, s0=None):
+    """The reference's debug entry (kernels/torch_binding.cpp:119-124, views carved at :57-84):
+    [o, sf, w, u, de, eg, ed, gl, Sc, M, T, A, T_post_leaf], per chunk and fp32:
+
+    * w [B,HV,NC,64,DV] = T (v beta), u [B,HV,NC,64,DK] = T (k beta e^c) (chunk_delta_cuda.cu:268-282);
+    * de [B,HV,NC,64,64] = e^{c_i - c_j} for i >= j else 0, eg = e^c, ed = e^{c_L - c} [B,HV,NC,64],
+      gl = e^{c_L} [B,HV,NC] (:284-294);
+    * Sc [B,HV,NC,DK,DV] the chunk-entry states; M = scale (q k^T) de (:480-509);
+    * T = (I - A)^-1, A the assembled strict-lower -(beta k k^T) de (:158-175), and T_post_leaf:
+      T after its 16 x 16 diagonal leaves are inverted, the other blocks still holding A (:176-214).
+
+    o, sf, T, u (= this kernel's W), Sc and the cumsum c behind the decay terms are the kernel's
+    own dumps (``chunk_prefill_debug_native``); w, A, M and the leaf stage, which this kernel does
+    not form in that shape (its U enters C12 through T' = T diag(beta), its inverse is not a leaf
+    doubling), are formed from those dumps and the inputs with fp32 tensor ops on the same device.
+    """
+    o, sf, c, T, W, _vnew, _of, sc = _run_prefill(q, k, v, g, beta, s0, debug=True)
+    B, T_len, HQK, HV = q.shape[0], q.shape[1], q.shape[2], v.shape[2]
+    NC = c.shape[2]
+    pad = NC * CHUNK - T_len
+
+    def chunked(x):  # [B, T, H, D] -> [B, HV, NC, 64, D] fp32, zero tail, heads expanded h // (HV / HQK)
+        x = torch.nn.functional.pad(x.float().permute(0, 2, 1, 3), (0, 0, 0, pad))
+        x = x.reshape(B, x.shape[1], NC, CHUNK, x.shape[-1])
+        return x.repeat_interleave(HV // x.shape[1], dim=1) if x.shape[1] != HV else x
+
+    kc, qc, vc = chunked(k), chunked(q), chunked(v)
+    bc = torch.nn.functional.pad(beta.float().permute(0, 2, 1), (0, pad)).reshape(B, HV, NC, CHUNK)
+    c = c.float()
+    tri = torch.ones(CHUNK, CHUNK, dtype=torch.bool, device=c.device).tril()
+    strict = tri.tril(-1)
+    diff = c[..., :, None] - c[..., None, :]
+    de = torch.where(tri, torch.exp(torch.where(tri, diff, torch.zeros_like(diff))), torch.zeros_like(diff))
+    eg = torch.exp(c)
+    ed = torch.exp(c[..., -1:] - c)
+    gl = torch.exp(c[..., -1]).contiguous()
+    kk = kc @ kc.transpose(-1, -2)
+    A = torch.where(strict, -(bc[..., None] * kk) * de, torch.zeros_like(kk))
+    M = (qc @ kc.transpose(-1, -2)) * de * (1.0 / HEAD_DIM ** 0.5)
+    w = T @ (vc * bc[..., None])
+    post = A.clone()
+    eye16 = torch.eye(16, dtype=torch.float32, device=c.device)
+    for bl in range(CHUNK // 16):
+        blk = slice(16 * bl, 16 * bl + 16)
+        post[..., blk, blk] = torch.linalg.solve_triangular(eye16 - A[..., blk, blk], eye16.expand_as(A[..., blk, blk]),
+                                                            upper=False, unitriangular=True)
+    return [o, sf, w, W, de, eg, ed, gl, sc, M, T, A, post]
 
 
 def chunk_prefill_gated(q, k, v, g, beta, z, w, s0=None, eps: float = 1e-6):

@@ -74,7 +74,7 @@ def test_stages_against_oracle_intermediates():
     inp = make_inputs(1, 150, 1, 2, 128, seed=11, dist="refgrid", with_s0=True)
     q, k, v = dev(inp.q), dev(inp.k), dev(inp.v)
     g, b, s = dev(inp.g, torch.float32), dev(inp.beta, torch.float32), dev(inp.s0, torch.float32)
-    out = gdn_b200.chunk_prefill_debug(q, k, v, g, b, s)
+    out = gdn_b200.chunk_prefill_debug_native(q, k, v, g, b, s)
     torch.cuda.synchronize()
     o, sf, c, T, W, vnew, of, sc = (host(t) for t in out)
     inter = {}
@@ -95,6 +95,39 @@ def test_stages_against_oracle_intermediates():
     assert errs["v_new"] < 1e-3
     assert errs["o"] < 1e-4
     check_o(o, o_ref, sf, sf_ref, "debug-run")
+
+
+def test_reference_debug_views():
+    """chunk_prefill_debug returns the reference debug entry's list (kernels/torch_binding.cpp:57-84):
+    [o, sf, w, u, de, eg, ed, gl, Sc, M, T, A, T_post_leaf] with its shapes, each view against the
+    oracle's restatement of what the reference kernel writes there (kernels/chunk_delta_cuda.cu).
+    A ragged tail (T = 150: three chunks, the last of 22 tokens) and 2 v-heads per qk-head."""
+    inp = make_inputs(1, 150, 1, 2, 128, seed=12, dist="refgrid", with_s0=True)
+    q, k, v = dev(inp.q), dev(inp.k), dev(inp.v)
+    g, b, s = dev(inp.g, torch.float32), dev(inp.beta, torch.float32), dev(inp.s0, torch.float32)
+    out = gdn_b200.chunk_prefill_debug(q, k, v, g, b, s)
+    torch.cuda.synchronize()
+    assert len(out) == 13
+    B, HV, NC, C, D = 1, 2, 3, 64, 128
+    shapes = [(B, 150, HV, D), (B, HV, D, D), (B, HV, NC, C, D), (B, HV, NC, C, D), (B, HV, NC, C, C),
+              (B, HV, NC, C), (B, HV, NC, C), (B, HV, NC), (B, HV, NC, D, D), (B, HV, NC, C, C),
+              (B, HV, NC, C, C), (B, HV, NC, C, C), (B, HV, NC, C, C)]
+    assert [tuple(t.shape) for t in out] == shapes
+    o, sf, w, u, de, eg, ed, gl, sc, M, T, A, post = (host(t) for t in out)
+    inter = {}
+    o_ref, sf_ref = O.chunk_gated_delta_rule(inp.q, inp.k, inp.v, inp.g, inp.beta, 64, inp.s0, intermediates=inter)
+    errs = {"w": tensor_l2_rel(w, inter["value"]), "u": tensor_l2_rel(u, inter["W"]),
+            "de": max_abs(de, inter["decay"]), "eg": max_abs(eg, inter["eg"]), "ed": max_abs(ed, inter["ed"]),
+            "gl": max_abs(gl, inter["gl"]), "Sc": tensor_l2_rel(sc, inter["S_entry"]),
+            "M": tensor_l2_rel(M, inter["M"]), "T": max_abs(T, inter["T"]), "A": tensor_l2_rel(A, inter["A"]),
+            "T_post_leaf": tensor_l2_rel(post, inter["T_post_leaf"])}
+    print({k_: f"{v_:.3e}" for k_, v_ in errs.items()})
+    for key in ("de", "eg", "ed", "gl"):
+        assert errs[key] < 1e-5, (key, errs[key])
+    assert errs["T"] < 1e-4
+    for key in ("w", "u", "Sc", "M", "A", "T_post_leaf"):
+        assert errs[key] < 1e-3, (key, errs[key])
+    check_o(o, o_ref, sf, sf_ref, "debug-views")
 
 
 # ------------------------------------------------------------------ golden vectors
