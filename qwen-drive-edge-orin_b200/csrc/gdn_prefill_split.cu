@@ -54,6 +54,7 @@ constexpr int ISSUER_WARP = NCOMPUTE / 32;
 constexpr int LAUNCH_REGS = 168, COMPUTE_REGS = 192, ISSUE_REGS = 120;
 static_assert(2 * 128 * COMPUTE_REGS + 128 * ISSUE_REGS <= NTHREADS * LAUNCH_REGS, "register split exceeds the pool");
 constexpr uint32_t CSYNC = 1;            // named barrier of warps 0-7
+constexpr uint32_t GSYNC = 2;            // named barrier of warpgroup 2 (output CTA: the gate warps)
 constexpr int NP = 2;                    // prep CTAs per cluster
 // Cluster ranks 2r and 2r+1 land on neighbouring SMs (one TPC). The kernel is sensitive to
 // instruction fetch (its hot loops exceed an SM's instruction cache), and it ran faster
@@ -108,8 +109,9 @@ constexpr uint32_t P_MISC = P_GATE + 2 * GSLOT;
 constexpr uint32_t U_OSLOT = 0;                  // 2 o^T slots (chunk parity), filled by the chain CTA
 constexpr uint32_t U_Z = 2 * O_BYTES;            // 2 z tiles (chunk parity)
 constexpr uint32_t U_OT = U_Z + 2 * O_BYTES;     // o [64 tok][128 dv] (two 64-row panels), transposed here
-constexpr uint32_t U_GATE = U_OT + O_BYTES;      // w * silu(z) fp32 [64 tok][128 dv], 16-byte chunks swizzled
-constexpr uint32_t U_MISC = U_GATE + 2 * O_BYTES;
+constexpr uint32_t U_GATE = U_OT + O_BYTES;      // 2 gate tiles (chunk parity): w * silu(z) fp32 [64 tok][128 dv],
+constexpr uint32_t GATE_BYTES = 2 * O_BYTES;     //   16-byte chunks swizzled
+constexpr uint32_t U_MISC = U_GATE + 2 * GATE_BYTES;
 // ---- misc (all roles; the chain keeps e^c of chunks with even / odd index at M_C, 128 floats)
 constexpr uint32_t M_C = 0, M_W = 512, M_BAR = 1024, M_TMEM = 1280, M_FLAG = 1284, M_DONE = 1288,
                    M_BYTES = 1408;
@@ -135,10 +137,11 @@ enum {
     B_TSFREE = B_DRAIN2 + 1 /* chain: dS read by the state update (one arrival per thread) */,
     B_EMPTYA = 11 /* prep */, B_EMPTYB = 12 /* prep */,
     B_GREADY = 13 /* prep: 2, gate slot written (32 arrivals) */, B_GFREE = 15 /* prep: 2, gate slot read */,
-    B_FULLO = 11 /* output: 2 */, B_ZT = 13 /* output: 2 */
+    B_FULLO = 11 /* output: 2 */, B_ZT = 13 /* output: 2 */,
+    B_OGFULL = 15 /* output: 2, gate tile written */, B_OGFREE = 17 /* output: 2, gate tile read */
 };
 constexpr int NBAR = B_TSFREE + 1;
-static_assert(B_GFREE + 2 <= NBAR, "prep barriers exceed the barrier area");
+static_assert(B_GFREE + 2 <= NBAR && B_OGFREE + 2 <= NBAR, "prep and output barriers exceed the barrier area");
 static_assert(M_BAR + 8 * NBAR <= M_TMEM, "barriers overlap the TMEM address word");
 
 // ---- TMEM
@@ -664,51 +667,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             }
         } else {
             // ---------------- output CTA: gated-RMSNorm epilogue of every chunk (4 threads per
-            // token, 16-byte chunks {eq, eq+4, eq+8, eq+12}); o arrives from the chain CTA
+            // token, 16-byte chunks {eq, eq+4, eq+8, eq+12}); o arrives from the chain CTA, the gate
+            // tile w * silu(z) from the gate warps (warpgroup 2), a chunk or two ahead
             const int et = tid >> 2, eq = tid & 3;
-            if (tid < HD) w_s[tid] = p.gated ? __bfloat162float(p.w[tid]) : 0.f;
-            csync();  // w_s visible to every thread (the first gate tile reads it)
-            auto load_zt = [&](int n) {
-                if (n & 1) load_tile(B_ZT + 1, U_Z + O_BYTES, &p.tm_z, h, n, armed_z1);
-                else load_tile(B_ZT, U_Z, &p.tm_z, h, n, armed_z0);
-            };
-            if (tid == 0 && p.gated)
-                for (int s = 0; s < 2 && s < NC; ++s) load_zt(s);
             for (int n = 0; n < NC; ++n) {
                 if (vote_abort()) break;
                 const int valid = min(CS, len - n * CS);
                 const long long tok0 = tok_base + (long long)n * CS;
                 const uint32_t par = (uint32_t)((n >> 1) & 1);
                 const uint32_t oslot = U_OSLOT + (uint32_t)(n & 1) * O_BYTES;
-                const uint32_t zt = U_Z + (uint32_t)(n & 1) * O_BYTES;
-                if (p.gated) {
-                    // gate = w * silu(z) of chunk n, formed while this CTA waits for o(n) from the chain (the
-                    // SFU-bound part of the epilogue is then off the last chunk's path); then z(n + 2) loads
-                    wait_bar(B_ZT + (n & 1), par);
-                    for (int u = tid; u < CS * 16; u += NCOMPUTE) {
-                        const int r = u >> 4, zc = u & 15;
-                        uint32_t w4[4];
-                        ld_shared_v4(sb + zt + sw_chunk(r, zc, 64), w4[0], w4[1], w4[2], w4[3]);
-                        float gv[8];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
-                            const float z0 = __low2float(z2), z1 = __high2float(z2);
-                            gv[2 * e] = w_s[8 * zc + 2 * e] * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
-                            gv[2 * e + 1] = w_s[8 * zc + 2 * e + 1] * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
-                        }
-                        *reinterpret_cast<float4*>(smem + U_GATE + gate_chunk(r, 2 * zc)) =
-                            make_float4(gv[0], gv[1], gv[2], gv[3]);
-                        *reinterpret_cast<float4*>(smem + U_GATE + gate_chunk(r, 2 * zc + 1)) =
-                            make_float4(gv[4], gv[5], gv[6], gv[7]);
-                    }
-                    csync();  // gate tile written; z tile read
-                    if (tid == 0 && !*abort_flag && n + 2 < NC) {  // this parity's z tile takes chunk n + 2
-                        ptx::fence_proxy_async_smem();
-                        load_zt(n + 2);
-                        prefetch_tile(&p.tm_z, h, n + 3);
-                    }
-                }
+                const uint32_t gate = U_GATE + (uint32_t)(n & 1) * GATE_BYTES;
                 wait_bar(B_FULLO + (n & 1), par);
                 {   // o^T -> o: thread (dv, token half) reads four 16-byte chunks of row dv
                     const int dv = tid >> 1, th = tid & 1;
@@ -753,6 +721,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 #pragma unroll
                     for (int j = 0; j < 16; ++j) outw[j] = pack_bf16(o[2 * j], o[2 * j + 1]);
                 } else {
+                    wait_bar(B_OGFULL + (n & 1), par);  // this chunk's gate tile
                     float ss = 0.f;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) ss = fmaf(o[j], o[j], ss);
@@ -762,8 +731,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 #pragma unroll
                     for (int m = 0; m < 4; ++m) {
                         const int c = eq + 4 * m;
-                        const float4 g0 = *reinterpret_cast<const float4*>(smem + U_GATE + gate_chunk(et, 2 * c));
-                        const float4 g1 = *reinterpret_cast<const float4*>(smem + U_GATE + gate_chunk(et, 2 * c + 1));
+                        const float4 g0 = *reinterpret_cast<const float4*>(smem + gate + gate_chunk(et, 2 * c));
+                        const float4 g1 = *reinterpret_cast<const float4*>(smem + gate + gate_chunk(et, 2 * c + 1));
                         const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
@@ -779,13 +748,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                         dst[eq + 4 * m] = make_uint4(outw[4 * m], outw[4 * m + 1], outw[4 * m + 2], outw[4 * m + 3]);
                 }
                 csync();  // o tile and gate tile read
+                if (tid == 0 && p.gated) ptx::mbar_arrive(bar(B_OGFREE + (n & 1)));  // the gate warps may refill it
             }
-            // Abort path: wait (bounded) for the z loads and the chain's o copies armed here
+            // Abort path: wait (bounded) for the chain's o copies armed here
             if (*abort_flag && tid == 0) {
                 drain(B_FULLO, armed_o0);
                 drain(B_FULLO + 1, armed_o1);
-                drain(B_ZT, armed_z0);
-                drain(B_ZT + 1, armed_z1);
             }
         }
         // Abort path: wait (bounded) for the TMA loads and MMAs this thread issued before
@@ -804,6 +772,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
         const bool producer = chain && warp == ISSUER_WARP + 1;
         const bool mma_out = chain && warp == ISSUER_WARP + 2;
         const bool gate_warp = !chain && !outcta && warp == ISSUER_WARP;
+        const bool out_gate = outcta && p.gated;  // warpgroup 2 of the output CTA forms the gate tiles
         auto prep_bar = [&](int b, int m) {  // the prep CTAs' barriers sit at their own misc offset
             return ptx::mapa(sb + P_MISC + M_BAR + 8u * (uint32_t)b, (uint32_t)(PREP_RANK0 + m % NSLOT));
         };
@@ -997,6 +966,59 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 gs[3 * CS + 2 * lane] = ex2f((cL - c0) * LOG2E);
                 gs[3 * CS + 2 * lane + 1] = ex2f((cL - c1) * LOG2E);
                 ptx::mbar_arrive(bar(B_GREADY + (k & 1)));  // every lane: its stores are released
+            }
+            __syncwarp();
+        } else if (out_gate) {
+            // ---------------- output CTA, warpgroup 2: the gate tile w * silu(z) of every chunk (SFU-bound)
+            // into one of two tiles (chunk parity), up to two chunks ahead of warps 0-7, which then run
+            // only the transpose and the norm. Thread 256 issues the z loads (two tiles, chunk parity).
+            const int gt = tid - ISSUER_WARP * 32;  // 0..127
+            auto gsync = [] { ptx::named_sync(GSYNC, 128); };
+            auto load_zt = [&](int n) {
+                if (n & 1) load_tile(B_ZT + 1, U_Z + O_BYTES, &p.tm_z, h, n, armed_z1);
+                else load_tile(B_ZT, U_Z, &p.tm_z, h, n, armed_z0);
+            };
+            w_s[gt] = __bfloat162float(p.w[gt]);
+            if (gt == 0)
+                for (int s = 0; s < 2 && s < NC; ++s) load_zt(s);
+            gsync();  // w_s visible to the four warps
+            for (int n = 0; n < NC; ++n) {
+                if (ptx::named_sync_or(GSYNC, 128, *abort_flag != 0)) break;  // one decision for the four warps
+                const uint32_t par = (uint32_t)((n >> 1) & 1);
+                // the tile was read by chunk n-2's epilogue, and z(n) has landed (a failed wait skips the
+                // work but not the barrier below, which every thread of the four warps reaches)
+                bool ok = n < 2 || wait_bar(B_OGFREE + (n & 1), (uint32_t)(((n >> 1) - 1) & 1));
+                ok = ok && wait_bar(B_ZT + (n & 1), par);
+                const uint32_t zt = U_Z + (uint32_t)(n & 1) * O_BYTES;
+                const uint32_t gate = U_GATE + (uint32_t)(n & 1) * GATE_BYTES;
+                for (int u = gt; ok && u < CS * 16; u += 128) {
+                    const int r = u >> 4, zc = u & 15;
+                    uint32_t w4[4];
+                    ld_shared_v4(sb + zt + sw_chunk(r, zc, 64), w4[0], w4[1], w4[2], w4[3]);
+                    float gv[8];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[e]);
+                        const float z0 = __low2float(z2), z1 = __high2float(z2);
+                        gv[2 * e] = w_s[8 * zc + 2 * e] * (z0 * rcpf(1.f + ex2f(-z0 * LOG2E)));
+                        gv[2 * e + 1] = w_s[8 * zc + 2 * e + 1] * (z1 * rcpf(1.f + ex2f(-z1 * LOG2E)));
+                    }
+                    *reinterpret_cast<float4*>(smem + gate + gate_chunk(r, 2 * zc)) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+                    *reinterpret_cast<float4*>(smem + gate + gate_chunk(r, 2 * zc + 1)) = make_float4(gv[4], gv[5], gv[6], gv[7]);
+                }
+                gsync();  // the gate tile is written and the z tile read by all four warps
+                if (gt == 0 && !*abort_flag) {
+                    ptx::mbar_arrive(bar(B_OGFULL + (n & 1)));  // (after the barrier: every gate store precedes it)
+                    if (n + 2 < NC) {                        // this parity's z tile takes chunk n + 2
+                        ptx::fence_proxy_async_smem();
+                        load_zt(n + 2);
+                        prefetch_tile(&p.tm_z, h, n + 3);
+                    }
+                }
+            }
+            if (gt == 0 && *abort_flag) {  // the z loads this thread armed, before the CTA leaves
+                drain(B_ZT, armed_z0);
+                drain(B_ZT + 1, armed_z1);
             }
             __syncwarp();
         } else {
