@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 }
                 const float* ecm = ecl + (m & 1) * CS;
                 const uint32_t ob = sb + C_OST + (uint32_t)(m & 1) * O_BYTES;
-#pragma unroll
+#pragma unroll 1
                 for (int h2 = 0; h2 < 2; ++h2) {  // 16 columns at a time (registers: the state is live)
                     float v[16], v2[16];
                     ptx::tmem_ld16(tl + T_O + 32 * half + 16 * h2, v);
@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                     const uint32_t sp = aslot(n);
                     const float* ed_s = reinterpret_cast<const float*>(smem + sp + A_ED);
                     // 16 columns at a time (the state is live in registers)
-#pragma unroll
+#pragma unroll 1
                     for (int hq = 0; hq < 2; ++hq) {
                         float v[16];
                         {
