@@ -147,6 +147,14 @@ constexpr int DBG_C = 0, DBG_T = 64, DBG_W = DBG_T + 4096, DBG_VN = DBG_W + 8192
 //   (P1) but takes T' and W^T from the records (no L, inverse, T'/T'' split or P3). Only the last
 //   segment of each sequence writes its final state, at sf[b].
 constexpr int SEG_NONE = 0, SEG_OUTPUT = 1, SEG_STATE = 2, SEG_PHI = 3;
+
+// A bounded wait that ran out: set the CTA's abort flag and record bits 0 and 15 (this kernel) in the
+// status word. Out of line: it runs only after a timeout, and inlined at each wait site it would put
+// cold code between the hot loop's instructions (the kernel is sensitive to instruction fetch).
+__device__ __noinline__ void record_failure_fused(volatile int* abort_flag, unsigned int* status) {
+    *abort_flag = 1;
+    if (status) atomicOr(status, 1u | (1u << 15));
+}
 template <bool kPrestage, bool kDebug, int kSeg = SEG_NONE>
 __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_constant__ Params p) {
     constexpr bool kState = (kSeg == SEG_STATE);
@@ -309,10 +317,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_kernel(const __grid_c
     // A failure is recorded as bit 0 plus bit 15 (this kernel) of the status word. Loads are
     // issued only while no failure is recorded: after a failed wait the phase waited for may
     // still be pending, and a new load would arm it a second time.
-    auto fail = [&]() {
-        *abort_flag = 1;
-        if (p.status) atomicOr(p.status, 1u | (1u << 15));
-    };
+    auto fail = [&]() { record_failure_fused(abort_flag, p.status); };
     auto wait_bar = [&](int i, uint32_t parity) {
         if (ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) ++consumed[i];
         else fail();

@@ -154,6 +154,20 @@ constexpr uint32_t T_VN_HI = 0, T_VN_LO = 32, T_VP_HI = 64, T_VP_LO = 96, T_O = 
 // prep: [0,64) P1; [128,256) P3 [T''_hi | T''_lo] parts of W^T
 constexpr uint32_t T_P = 0, T_W = 128;
 
+// A bounded wait that ran out: set the CTA's abort flag and record bit 0 plus the role that gave up
+// in the status word. Out of line: it runs only after a timeout, and inlined at each of the kernel's
+// many wait sites it would put cold code between the hot loops' instructions (the kernel is
+// sensitive to instruction fetch).
+__device__ __noinline__ void record_failure(volatile int* abort_flag, unsigned int* status) {
+    *abort_flag = 1;
+    if (status) {  // the role, from the thread and the CTA's rank
+        const uint32_t w = threadIdx.x >> 5, r = ptx::cluster_ctarank();
+        const uint32_t role = r == CHAIN_RANK ? (w < (uint32_t)ISSUER_WARP ? 8u : 9u + (w - ISSUER_WARP))
+                                              : (r == OUT_RANK ? 14u : (w < (uint32_t)ISSUER_WARP ? 12u : 13u));
+        atomicOr(status, 1u | (1u << role));
+    }
+}
+
 // kSeg: the instantiation for the passes of a segmented call (segment indexing, the state
 // pass's identity runs, last-segment final states); the plain instantiation carries none of it.
 template <bool kSeg>
@@ -245,15 +259,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     // thread roles leave their loop at once; warps 0-7, which share named barriers, carry on to
     // their next vote (their own arrivals are on count barriers without transaction bytes) and
     // leave together.
-    auto fail = [&]() {
-        *abort_flag = 1;
-        if (p.status) {  // the role, recomputed here (cold path) rather than kept in a register
-            const uint32_t w = threadIdx.x >> 5, r = ptx::cluster_ctarank();
-            const uint32_t role = r == CHAIN_RANK ? (w < (uint32_t)ISSUER_WARP ? 8u : 9u + (w - ISSUER_WARP))
-                                                  : (r == OUT_RANK ? 14u : (w < (uint32_t)ISSUER_WARP ? 12u : 13u));
-            atomicOr(p.status, 1u | (1u << role));
-        }
-    };
+    auto fail = [&]() { record_failure(abort_flag, p.status); };
     auto wait_bar = [&](int i, uint32_t parity) -> bool {
         if (ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) return true;
         fail();
