@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     // leave together.
     auto fail = [&]() { record_failure(abort_flag, p.status); };
     auto wait_bar = [&](int i, uint32_t parity) -> bool {
-        if (ptx::mbar_wait(bar(i), parity, WAIT_ITERS)) return true;
+        if (ptx::mbar_wait_compact(bar(i), parity, WAIT_ITERS)) return true;
         fail();
         return false;
     };
@@ -274,11 +274,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
     // abort path: wait (bounded) for the last phase armed on a barrier (re-armed only after
     // its previous phase was consumed), and for every MMA this thread issued
     auto drain = [&](int b, uint32_t armed) {
-        if (armed > 0) ptx::mbar_wait(bar(b), (armed - 1) & 1u, WAIT_ITERS);
+        if (armed > 0) ptx::mbar_wait_compact(bar(b), (armed - 1) & 1u, WAIT_ITERS);
     };
     auto drain_mma = [&](int b) {
         ptx::mma_commit(bar(b));
-        ptx::mbar_wait(bar(b), 0u, WAIT_ITERS);
+        ptx::mbar_wait_compact(bar(b), 0u, WAIT_ITERS);
     };
     auto commit = [&]() { commit_to(B_MMA); };
     auto csync = [] { ptx::named_sync(CSYNC, NCOMPUTE); };
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
                 ptx::tc_fence_after();
                 // the output CTA has handed back this buffer (its chunk m - 2)
                 bool handed_back = true;
-                if (m >= 2 && !ptx::mbar_wait(bar(B_EMPTYO + (m & 1)), (uint32_t)(((m >> 1) - 1) & 1), WAIT_ITERS)) {
+                if (m >= 2 && !ptx::mbar_wait_compact(bar(B_EMPTYO + (m & 1)), (uint32_t)(((m >> 1) - 1) & 1), WAIT_ITERS)) {
                     fail();
                     handed_back = false;
                 }
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
 
                 // ---- v_new hi/lo and (v_new e^{cL-c}) hi/lo -> TMEM A operands; keep e^c
                 wait_mma(ph);
-                if (!ptx::mbar_wait(bar(B_FULLA + n % NSLOT), slot_par(n), WAIT_ITERS)) fail();  // decay factors landed
+                if (!ptx::mbar_wait_compact(bar(B_FULLA + n % NSLOT), slot_par(n), WAIT_ITERS)) fail();  // decay factors landed
                 {
                     const uint32_t sp = aslot(n);
                     const float* ed_s = reinterpret_cast<const float*>(smem + sp + A_ED);
@@ -668,7 +668,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_prefill_split_kernel(const __
             if (tid == 0 && k >= 1 && !*abort_flag) {  // the last shipment must land before this CTA exits
 #pragma unroll
                 for (int b = B_EMPTYA; b <= B_EMPTYB; ++b) {
-                    if (!ptx::mbar_wait(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) fail();
+                    if (!ptx::mbar_wait_compact(bar(b), (uint32_t)((k - 1) & 1), WAIT_ITERS)) fail();
                 }
             }
         } else {

@@ -69,6 +69,32 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     return false;
 }
 
+// The same bounded wait as one compact block of inline PTX (block-scoped labels, no backoff sleep:
+// a try_wait suspends the thread while the phase is pending, so max_iters polls still bound the
+// wait in time). It is smaller at each inlined wait site, which measured faster in the cluster-split
+// kernel, whose hot loops are limited by instruction fetch on some SMs, and slower in the
+// one-CTA-per-head kernel (block-wide waits), which keeps mbar_wait.
+__device__ __forceinline__ bool mbar_wait_compact(uint32_t bar, uint32_t parity, uint32_t max_iters) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .u32 it;\n\t"
+        "mov.u32 it, 0;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "@p bra DONE;\n"
+        "POLL:\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "@p bra DONE;\n\t"
+        "add.u32 it, it, 1;\n\t"
+        "setp.lt.u32 p, it, %3;\n\t"
+        "@p bra POLL;\n"
+        "DONE:\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(max_iters)
+        : "memory");
+    return ok != 0;
+}
+
 // Programmatic dependent launch: wait until the grids this launch depends on have completed
 // and their memory is visible (a no-op without such a dependency), then let the next launch
 // in the stream be scheduled: its CTAs take SMs as this grid's CTAs leave them and run up to
